@@ -1,0 +1,478 @@
+"""Benchmark of the fused mixed-precision optimizer step (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload qwen3_8b] [--impl ours]
+
+One "step" is the reference's optimizer step (train.py:485-491) through this package's public
+API: ``GradScaler.unscale_`` -> ``clip_grad_norm_`` -> ``GradScaler.step`` -> ``update`` over
+the whole parameter list of the workload, with the optimizer state resident in HBM.  At N=1 it
+is :class:`FusedAdamW`; at N>1 (torchrun, one rank per GPU, NCCL) it is the ZeRO-1
+:class:`ZeroAdamW`, each rank updating its contiguous 1/N shard.
+
+Printed by rank 0: one JSON line with ``value`` = Gparams/s of the timed steps (device time,
+max over ranks), the roofline of the AdamW kernel, the end-to-end number through host buffers,
+the CPU baseline (the reference's torch CPU chain on the host cores), clocks and launch count.
+``--impl reference`` times only the reference's CPU chain, on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from minigpt_train_infra_b200 import workloads  # noqa: E402
+
+METRIC = "fused AdamW step Gparams/s and HBM GB/s vs peak at 1/2/4/8 B200"
+ADAMW_BYTES = 28   # read g(2)+w,m,v(12); write w,m,v(12)+bf16 param(2)
+STATS_BYTES = 2    # read g
+FALLBACK_HBM_GBS = 6650.0
+LR, BETAS, EPS, WD, CLIP = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
+SCALES = {"qwen3_8b": 2.0 ** 15}
+GRAD_STD = {"flat_2_28": 1e-2}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+# peaks and clocks
+# ------------------------------------------------------------------------------------------
+
+def hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """NVML samples of SM clock and throttle reasons while the timed region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, device_index: int, period: float = 0.05):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            uuid = None
+            try:
+                uuid = torch.cuda.get_device_properties(device_index).uuid
+            except Exception:
+                pass
+            self._h = None
+            if uuid is not None:
+                try:
+                    self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + str(uuid)).encode())
+                except Exception:
+                    self._h = None
+            if self._h is None:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[device_index]) if vis else device_index
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception as e:  # NVML missing: report no clock data rather than fail
+            log("clock sampling unavailable:", e)
+        self.period = period
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._ok:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._ok:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------
+# workload setup
+# ------------------------------------------------------------------------------------------
+
+def make_model_params(shape_list, device) -> tuple[list, list]:
+    params, groups = [], []
+    for _, shape, g in shape_list:
+        params.append(torch.nn.Parameter(torch.empty(shape, dtype=torch.bfloat16, device=device)))
+        groups.append(g)
+    return params, groups
+
+
+def fill_seeded(t: torch.Tensor, seed: int, std: float, absval: bool = False) -> None:
+    """Seeded N(0, std) (or |N(0,1)|*std) fill, generated on the device tensor by tensor."""
+    gen = torch.Generator(device=t.device).manual_seed(seed)
+    flat = t.view(-1)
+    step = 1 << 28
+    for k, s in enumerate(range(0, flat.numel(), step)):
+        part = flat[s:s + step]
+        tmp = torch.empty(part.numel(), dtype=torch.float32, device=t.device)
+        tmp.normal_(0.0, 1.0, generator=gen)
+        if absval:
+            tmp.abs_()
+        tmp.mul_(std)
+        part.copy_(tmp)
+        del tmp
+
+
+def seed_state(opt, params, step0: float = 999.0) -> None:
+    """Config-2 state: master ~ N(0,0.02), m ~ N(0,1e-3), v = |N(0,1)|*1e-6, step 999."""
+    store = opt._ensure_store()
+    opt._sync_state()
+    fill_seeded(store.master, 1, 0.02)
+    fill_seeded(store.exp_avg, 2, 1e-3)
+    fill_seeded(store.exp_avg_sq, 3, 1e-6, absval=True)
+    store.steps.fill_(step0)
+    with torch.no_grad():
+        for slot, p in enumerate(store.params):
+            mp = store.views[slot].get("master_param")
+            if mp is not None:
+                p.copy_(mp)
+
+
+def make_grads(params, scale: float, std: float, seed: int = 7) -> list[torch.Tensor]:
+    grads = []
+    for i, p in enumerate(params):
+        g = torch.empty_like(p)
+        fill_seeded(g, seed * 1000 + i, std * scale)
+        grads.append(g)
+    return grads
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the reference's torch CPU chain on a bounded sample of the same workload
+# ------------------------------------------------------------------------------------------
+
+def cpu_sample_shapes(shape_list, min_params: int = 1 << 27) -> list:
+    """The workload's tensors from the first 2-D weight on, until >= min_params (bounded)."""
+    out, tot = [], 0
+    for item in shape_list:
+        n = math.prod(item[1])
+        if tot >= min_params:
+            break
+        if n > 4 * min_params and tot == 0 and len(shape_list) > 1:
+            continue  # skip a vocabulary matrix so the sample stays bounded
+        out.append(item)
+        tot += n
+    return out
+
+
+def run_cpu_baseline(shape_list, scale: float, std: float, steps: int = 3, warmup: int = 1):
+    from oracle.torch_chain import ChainConfig, ReferenceChain, time_reference_chain
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = cpu_sample_shapes(shape_list)
+    n = sum(math.prod(s) for _, s, _ in sample)
+    gen = torch.Generator().manual_seed(11)
+    dec = [torch.randn(s, generator=gen) * 0.02 for _, s, g in sample if g == 0]
+    nod = [torch.randn(s, generator=gen) * 0.02 for _, s, g in sample if g == 1]
+    cfg = ChainConfig(lr=LR, betas=BETAS, eps=EPS, max_norm=CLIP, init_scale=scale)
+    chain = ReferenceChain([dec, nod], [WD, 0.0], cfg)
+    order = [s for _, s, g in sample if g == 0] + [s for _, s, g in sample if g == 1]
+    grads = [(torch.randn(s, generator=gen) * std * scale).to(torch.bfloat16) for s in order]
+    times = time_reference_chain(chain, grads, steps=steps, warmup=warmup)
+    med = statistics.median(times)
+    cpu_name = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                cpu_name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {
+        "value": n / med / 1e9, "unit": "Gparams/s", "cores": torch.get_num_threads(),
+        "kind": "reference",
+        "sample": (f"{len(sample)} tensors / {n:,} params of the workload (its first layers), "
+                   f"median of {steps} steps after {warmup} warm-up; torch {torch.__version__} "
+                   f"CPU AdamW(foreach=False,fused=False)+GradScaler('cpu')+clip_grad_norm_ in "
+                   f"the order of train.py:485-491, bf16 grads upcast and bf16 param copy "
+                   f"included; CPU: {cpu_name}"),
+        "seconds_per_step": med,
+    }
+
+
+# ------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_ours(args) -> None:
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+        pg = dist.group.WORLD
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    name = args.workload
+    shape_list = workloads.shapes(name)
+    P = workloads.n_params(name)
+    scale = SCALES.get(name, 2.0 ** 16)
+    std = GRAD_STD.get(name, 1e-3)
+    t0 = time.time()
+    params, gids = make_model_params(shape_list, device)
+    groups = [{"params": [p for p, g in zip(params, gids) if g == 0], "weight_decay": WD},
+              {"params": [p for p, g in zip(params, gids) if g == 1], "weight_decay": 0.0}]
+    groups = [g for g in groups if g["params"]]
+    if ws > 1:
+        from minigpt_train_infra_b200 import ZeroAdamW
+        opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=pg)
+        opt.seed_state_(master_std=0.02, m_std=1e-3, v_scale=1e-6, step=999.0)
+        grads = opt.make_flat_grads_()
+        fill_seeded(opt.flat_grad, 7, std * scale)
+        scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
+        step_params = opt.managed_params()
+    else:
+        opt = FusedAdamW(groups, lr=LR, betas=BETAS, eps=EPS)
+        seed_state(opt, params)
+        grads = make_grads(params, scale, std)
+        scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
+        step_params = params
+    for p, g in zip(params, grads):
+        p.grad = g
+    scaler.scale(torch.ones((), device=device))  # creates the scale tensor, as loss scaling does
+    torch.cuda.synchronize()
+    log(f"[rank {rank}] setup {time.time() - t0:.1f}s, {P:,} params, "
+        f"mem {torch.cuda.memory_allocated() / 2**30:.1f} GiB")
+
+    def one_step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        scaler.unscale_(opt)
+        clip_grad_norm_(step_params, CLIP)
+        if ev is not None:
+            ev[1].record()
+        scaler.step(opt)
+        if ev is not None:
+            ev[2].record()
+        scaler.update()
+        if ev is not None:
+            ev[3].record()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if pg is not None:
+        torch.distributed.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if pg is not None:
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+        for i in range(args.steps):
+            one_step(evs[i])
+        torch.cuda.synchronize()
+    total_ms = evs[0][0].elapsed_time(evs[-1][3])
+    stats_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    adamw_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    upd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    if pg is not None:
+        t = torch.tensor([total_ms, stats_ms, adamw_ms, upd_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms, stats_ms, adamw_ms, upd_ms = [float(x) for x in t.tolist()]
+    ms_per_step = total_ms / args.steps
+    value = P * args.steps / (total_ms / 1e3) / 1e9
+    P_local = opt.local_numel() if ws > 1 else P
+    peak, peak_kind = hbm_peak()
+    achieved = ADAMW_BYTES * P_local / (adamw_ms / 1e3) / 1e9
+    n_plans = len(opt._plans or [])
+    launches_per_step = (n_plans + (1 if n_plans > 1 else 0)) + n_plans + 1
+    if ws > 1:
+        launches_per_step += 1  # finalize of the exchanged partials
+
+    # end-to-end through the public API with host-resident gradients
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_baseline(shape_list, scale, std)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "Gparams/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded on device: master~N(0,0.02), m~N(0,1e-3), v=|N(0,1)|*1e-6,"
+                    f" bf16 grads~N(0,{std})*{scale:g})",
+            "config": {
+                "workload": f"{name}: {len(shape_list)} tensors, {P:,} params (BASELINE config "
+                            f"{ {'minigpt_6l_384': 1, 'flat_2_28': 2, 'gpt2_124m': 3, 'qwen3_1_7b': 4, 'qwen3_8b': 5}.get(name, '?') })",
+                "params": P, "params_per_rank": P_local,
+                "parallelism": "single GPU" if ws == 1 else f"zero1 over {ws} GPUs",
+                "timed": "unscale_+clip_grad_norm_+step+update per step" +
+                         (" (sharded update; bf16 all-gather reported under allgather)"
+                          if ws > 1 else ""),
+                "l2": "no flush: every step streams the whole optimizer state "
+                      f"({16 * P_local / 1e9:.1f} GB per rank), far above the 126 MB L2",
+                "hp": {"lr": LR, "betas": BETAS, "eps": EPS, "weight_decay": WD, "clip": CLIP,
+                       "loss_scale": scale},
+            },
+            "kernels_ms": {"grad_stats": round(stats_ms, 4), "adamw": round(adamw_ms, 4),
+                           "scaler_update": round(upd_ms, 4)},
+            "hbm_gbs": round((ADAMW_BYTES + STATS_BYTES) * P_local / (ms_per_step / 1e3) / 1e9, 1),
+            "hbm_frac": round((ADAMW_BYTES + STATS_BYTES) * P_local / (ms_per_step / 1e3) / 1e9
+                              / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": "b2o adamw_kernel", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": f"{peak_kind} copy bandwidth",
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "bytes_per_param": ADAMW_BYTES, "params_per_launch": P_local,
+                         "traffic": None},
+            "clocks": clocks.summary(),
+            "gpu_launches": launches_per_step * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        if ws > 1:
+            line["allgather"] = getattr(opt, "last_allgather_report", None)
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
+    """Same metric through the public API, gradients copied from pinned host memory each step
+    and the step's result (norm, found_inf, scale) read back to the host each step."""
+    from minigpt_train_infra_b200 import clip_grad_norm_
+    steps = max(2, min(args.steps, args.e2e_steps))
+    host = [torch.empty(g.shape, dtype=g.dtype, pin_memory=True) for g in grads]
+    for h, g in zip(host, grads):
+        h.copy_(g)
+    res_host = torch.empty(3, dtype=torch.float32, pin_memory=True)
+    h2d = sum(g.numel() * g.element_size() for g in grads)
+
+    def step():
+        for g, h in zip(grads, host):
+            g.copy_(h, non_blocking=True)
+        scaler.unscale_(opt)
+        norm = clip_grad_norm_(step_params, CLIP)
+        found = next(iter(scaler._per_optimizer_states[id(opt)]["found_inf_per_device"].values()))
+        scaler.step(opt)
+        res = torch.stack([norm.float(), found.float(), scaler._scale.float()])
+        scaler.update()
+        res_host.copy_(res, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    step()
+    if pg is not None:
+        torch.distributed.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if pg is not None:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    del host
+    return {"value": round(P * steps / (ms / 1e3) / 1e9, 3), "unit": "Gparams/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12, "steps": steps,
+            "ms_per_step": round(ms / steps, 3)}
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    name = args.workload
+    shape_list = workloads.shapes(name)
+    scale = SCALES.get(name, 2.0 ** 16)
+    std = GRAD_STD.get(name, 1e-3)
+    steps = max(1, min(args.steps, 5))
+    warmup = max(1, min(args.warmup, 2))
+    cpu = run_cpu_baseline(shape_list, scale, std, steps=steps, warmup=warmup)
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(cpu["value"], 4),
+        "unit": "Gparams/s", "n_gpus": ws, "steps": steps, "warmup": warmup,
+        "ms_per_step": round(cpu["seconds_per_step"] * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": f"{name}: bounded sample (see cpu_baseline.sample)",
+                   "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(cpu["value"], 4), "unit": "Gparams/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="qwen3_8b", choices=sorted(workloads.WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        log("note: fewer than 3 warm-up steps")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

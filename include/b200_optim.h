@@ -1,0 +1,192 @@
+/*
+ * b200_optim.h -- C ABI of the B200 fused mixed-precision optimizer step.
+ *
+ * The reference (TuraLucrs/minigpt-train-infra) runs this step through PyTorch
+ * (train.py:485-491):
+ *
+ *     scaler.unscale_(optimizer)          -> torch._amp_foreach_non_finite_check_and_unscale_
+ *     clip_grad_norm_(params, max_norm)   -> torch._foreach_norm, vector_norm, _foreach_mul_
+ *     scaler.step(optimizer)              -> torch._fused_adamw_ (CUDA) / _single_tensor_adam
+ *     scaler.update()                     -> torch._amp_update_scale_
+ *
+ * Each entry point below replaces one of those ATen operator calls; the comment of each names the
+ * torch Python line that issues the call it replaces (paths relative to the installed torch
+ * package).  The Python layer of this package (optim.py, amp.py, clip.py, zero1.py) binds them
+ * through ctypes; a C, C++ or other FFI host binds the same symbols directly.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless its comment says "host".
+ *  - Every launching entry point is asynchronous on `stream` (a cudaStream_t passed as void*),
+ *    performs no host synchronisation and allocates no memory.  Buffers are owned by the caller.
+ *  - Return value: B2O_OK (0) or a negative b2o_status.  Nothing aborts or traps.
+ *  - Calls that share a workspace must be ordered on one stream (not re-entrant per workspace).
+ */
+#ifndef B200_OPTIM_H_
+#define B200_OPTIM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2O_ABI_VERSION 1
+#define B2O_MAX_GROUPS 16
+#define B2O_VEC 8 /* elements per vector step: one 16-byte bf16 load, two 16-byte fp32 loads */
+
+typedef enum {
+  B2O_OK = 0,
+  B2O_ERR_ARG = -1,       /* null pointer, negative size, unknown dtype, too many groups   */
+  B2O_ERR_CAPACITY = -2,  /* an output array is too small for the plan                      */
+  B2O_ERR_LAUNCH = -3,    /* the kernel launch failed (cudaGetLastError)                    */
+  B2O_ERR_CUDA = -4,      /* another CUDA runtime call failed                               */
+  B2O_ERR_TABLE = -5      /* a tensor table entry is inconsistent (overlap, bad slot/group) */
+} b2o_status;
+
+typedef enum { B2O_BF16 = 0, B2O_F32 = 1 } b2o_dtype;
+
+/* One tensor (or, under ZeRO-1, the part of one tensor inside this rank's shard). */
+typedef struct b2o_tensor {
+  const void* grad;     /* gradient, dtype = grad_dtype of the call                          */
+  void* param;          /* bf16 model parameter to refresh from the master; NULL when the
+                           parameters are fp32 (then `master` is the parameter itself)      */
+  float* master;        /* fp32 master weights                                               */
+  float* exp_avg;       /* fp32 first moment                                                 */
+  float* exp_avg_sq;    /* fp32 second moment                                                */
+  int64_t numel;        /* elements in this slice (0 allowed)                                */
+  int32_t group;        /* index into the b2o_group array of the call                        */
+  int32_t slot;         /* per-parameter index: step counter and norm accumulator            */
+  int32_t chunk_begin;  /* written by b2o_plan_chunks                                        */
+  int32_t chunk_count;  /* written by b2o_plan_chunks                                        */
+  int32_t flags;        /* written by b2o_plan_chunks: B2O_FLAG_VECTOR when every pointer is
+                           16-byte aligned so the 128-bit path may be used                  */
+  int32_t reserved;
+} b2o_tensor;
+
+#define B2O_FLAG_VECTOR 1
+
+/* A contiguous element range [begin, end) of one tensor, processed by one CTA iteration. */
+typedef struct b2o_chunk {
+  int32_t tensor;
+  int32_t reserved;
+  int64_t begin;
+  int64_t end;
+} b2o_chunk;
+
+/* Hyper-parameters of one param_group, as the Python floats torch's AdamW holds. */
+typedef struct b2o_group {
+  double lr;
+  double beta1;
+  double beta2;
+  double eps;
+  double weight_decay;
+} b2o_group;
+
+/* ---------------------------------------------------------------------------------------- */
+/* Library identity                                                                          */
+/* ---------------------------------------------------------------------------------------- */
+
+/* ABI version this library was built with (B2O_ABI_VERSION). */
+int b2o_abi_version(void);
+
+/* Human-readable text of a b2o_status value (static storage). */
+const char* b2o_status_string(int status);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Multi-tensor-apply planning (host only)                                                   */
+/* Replaces the tensor-list chunking of ATen's multi_tensor_apply that                        */
+/* torch._amp_foreach_non_finite_check_and_unscale_ / torch._fused_adamw_ perform per call    */
+/* (issued from torch/amp/grad_scaler.py:294 and torch/optim/adam.py:880).                    */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Split every tensor of `tensors` (host array, n_tensors entries) into chunks of `chunk_elems`
+ * elements (a positive multiple of B2O_VEC), write them to `chunks` (host array, capacity
+ * `chunk_cap`) and the count to *n_chunks (host).  Fills chunk_begin, chunk_count and flags of
+ * each tensor entry.  Validates the table: non-null pointers for non-empty tensors, group in
+ * [0, n_groups), slot in [0, n_slots), no slot used twice.  Pass chunks == NULL to only count. */
+int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups, int32_t n_slots,
+                    int64_t chunk_elems, int32_t grad_dtype, b2o_chunk* chunks,
+                    int64_t chunk_cap, int64_t* n_chunks);
+
+/* Bytes of device workspace the stats pass needs for a plan (all calls of one optimizer share
+ * it): per-chunk partial sums, the per-slot exchange vector and two completion counters. */
+size_t b2o_workspace_bytes(int64_t n_chunks, int32_t n_slots);
+
+/* Zero the counters of a freshly allocated workspace (cudaMemsetAsync on `stream`). */
+int b2o_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Pass 1: unscale + non-finite check + L2 partial sums                                      */
+/* Replaces torch._amp_foreach_non_finite_check_and_unscale_ (torch/amp/grad_scaler.py:294)   */
+/* and torch._foreach_norm + linalg.vector_norm (torch/nn/utils/clip_grad.py:96,106).         */
+/* Gradients are read, never written: the unscale and clip factors are applied by pass 2.     */
+/* ---------------------------------------------------------------------------------------- */
+
+/* Reads every gradient once.  x = float(g) * inv_scale (fp32) with inv_scale =
+ * fp32(1 / double(*loss_scale)) -- GradScaler's `_scale.double().reciprocal().float()`
+ * (grad_scaler.py:351) -- or 1 when loss_scale is NULL; accumulates x*x per chunk and
+ * flags any non-finite g (tested before scaling, as torch does).  The last CTA to finish folds
+ * the chunk partials, in chunk order, into the per-slot exchange vector: exch[slot] (double) for
+ * every slot of the table and exch[n_slots] += 1.0 if a non-finite value was seen.
+ * `flags`:
+ *   B2O_STATS_CLEAR     zero exch[0..n_slots] first (the first table of a step);
+ *   B2O_STATS_FINALIZE  also write *found_inf_out (1.0f or 0.0f) and *norm_out (total norm,
+ *                       fp32) from exch, exactly as b2o_finalize_norm would for one rank.
+ * `exch` (n_slots+1 doubles) may be NULL to use the
+ * exchange area inside `workspace`. */
+#define B2O_STATS_FINALIZE 1
+#define B2O_STATS_CLEAR 2
+int b2o_grad_stats(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk* chunks,
+                   int64_t n_chunks, int32_t n_slots, int32_t grad_dtype,
+                   const float* loss_scale, void* workspace, double* exch, int32_t flags,
+                   float* found_inf_out, float* norm_out, void* stream);
+
+/* Fold `n_ranks` exchange vectors (laid out rank-major, n_slots+1 doubles each) in rank order:
+ * per-slot norm = fp32(sqrt(sum)), total = fp32(sqrt(sum of squared per-slot norms)), and
+ * found_inf = 1.0f if any rank saw a non-finite gradient.  One CTA; deterministic. */
+int b2o_finalize_norm(const double* exch_all, int32_t n_ranks, int32_t n_slots,
+                      float* found_inf_out, float* norm_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Pass 2: fused AdamW + bf16 parameter refresh                                              */
+/* Replaces torch._fused_adamw_ (torch/optim/adam.py:880) and, on the CPU path the reference  */
+/* runs, _single_tensor_adam (torch/optim/adam.py:347-552) plus clip_grad.py:174's            */
+/* torch._foreach_mul_ of the clip coefficient.                                               */
+/* ---------------------------------------------------------------------------------------- */
+
+/* For every element: g = (float(grad) * inv_scale) * clip_coef (inv_scale formed from
+ * *loss_scale exactly as in b2o_grad_stats), then the decoupled-weight-decay
+ * AdamW update of master/exp_avg/exp_avg_sq in the rounding order of torch's single-tensor
+ * AdamW, then param = bf16(master) when `param_dtype` is B2O_BF16.
+ *   steps[slot]     fp32 step counters (torch state["step"]); the update uses steps+1 and the
+ *                   last CTA stores steps+1 for every slot of the table.
+ *   found_inf       NULL or a device flag; non-zero skips the whole update, counters included.
+ *   loss_scale      NULL (factor 1) or the loss scale the gradients carry; the same pointer
+ *                   pass 1 read, unchanged in between.
+ *   norm, max_norm  when norm != NULL: clip_coef = min(max_norm / (norm + 1e-6), 1) rounded as
+ *                   torch/nn/utils/clip_grad.py:165-169 does; NULL means no clipping.
+ *   clip_coef_out   NULL or where to store the coefficient used (for reporting).
+ * `groups` is a host array of n_groups (<= B2O_MAX_GROUPS) entries, passed by value. */
+int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk* chunks,
+                   int64_t n_chunks, const b2o_group* groups, int32_t n_groups,
+                   int32_t grad_dtype, int32_t param_dtype, float* steps,
+                   const float* found_inf, const float* loss_scale, const float* norm,
+                   float max_norm, float* clip_coef_out, void* workspace, void* stream);
+
+/* ---------------------------------------------------------------------------------------- */
+/* Loss-scale update                                                                         */
+/* Replaces torch._amp_update_scale_ (torch/amp/grad_scaler.py:549).                          */
+/* ---------------------------------------------------------------------------------------- */
+
+/* If *found_inf != 0: scale *= backoff, tracker = 0.  Else tracker += 1 and, when it reaches
+ * growth_interval, scale *= growth (kept only if finite) and tracker = 0.  One thread. */
+int b2o_scaler_update(float* scale, int32_t* growth_tracker, const float* found_inf,
+                      double growth_factor, double backoff_factor, int32_t growth_interval,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200_OPTIM_H_ */

@@ -1,0 +1,233 @@
+// Pass 2 of the optimizer step: fused AdamW + bf16 parameter refresh (sm_100a).
+//
+// One read of grad (2 B bf16), master, exp_avg, exp_avg_sq (12 B) and one write of master,
+// exp_avg, exp_avg_sq (12 B) and the bf16 parameter (2 B) per element: 28 bytes, the HBM
+// roofline of this pass.  No tensor cores: the step is ~15 flops per 28 bytes.
+//
+// Per element, in the order and rounding of torch's single-tensor AdamW on the reference's
+// CPU path (torch/optim/adam.py:414-547, decoupled weight decay from torch/optim/adamw.py):
+//   g  = (float(grad) * inv_scale) * clip_coef          grad_scaler.py:294, clip_grad.py:174
+//   w  = w * fp32(1 - lr*wd)                            adam.py:419
+//   m  = fma(fp32(1-b1), g - m, m)                      adam.py:457 (lerp, weight < 0.5)
+//   v  = fma(fp32(1-b2) * g, g, v * fp32(b2))           adam.py:476 (mul_ then addcmul_)
+//   d  = sqrt(v) / fp32(sqrt(1 - b2^step)) + fp32(eps)  adam.py:536,545
+//   w  = w + (fp32(-lr/(1 - b1^step)) * m) / d          adam.py:534,547 (addcdiv_)
+//   p  = bf16_rne(w)                                    the mixed-precision parameter copy
+// The bias-correction scalars are formed in fp64 from the device step counter, as the
+// reference forms them in Python doubles from state["step"].
+//
+// Skipping: when *found_inf != 0 every CTA returns before touching memory, so a skipped step
+// moves ~0 bytes and leaves the step counters alone (GradScaler.step's skip, grad_scaler.py:
+// 363-374).  Otherwise the last CTA to finish stores step+1 for every slot of the table.
+#include <cuda_runtime.h>
+
+#include "b2o_device.cuh"
+#include "b2o_host.h"
+
+namespace b2o {
+
+struct GroupArgs {
+  b2o_group g[B2O_MAX_GROUPS];
+};
+
+struct ChunkScalars {
+  float decay, w1, w1m1, beta2, omb2, bc2_sqrt, neg_step_size, eps;
+  int small_w1;
+};
+
+__device__ __forceinline__ void chunk_scalars(const b2o_group& hp, float step_old,
+                                              ChunkScalars& s) {
+  // Python evaluates these in double, one rounding per operator; the explicit _rn forms keep
+  // nvcc from contracting `1 - lr*wd` into an fma.
+  const double step = (double)__fadd_rn(step_old, 1.0f);  // torch: step_t += 1 (fp32), .item()
+  const double bc1 = __dsub_rn(1.0, pow(hp.beta1, step));
+  const double bc2 = __dsub_rn(1.0, pow(hp.beta2, step));
+  s.decay = (float)__dsub_rn(1.0, __dmul_rn(hp.lr, hp.weight_decay));
+  s.w1 = (float)__dsub_rn(1.0, hp.beta1);
+  s.w1m1 = __fsub_rn(s.w1, 1.0f);
+  s.small_w1 = fabsf(s.w1) < 0.5f;
+  s.beta2 = (float)hp.beta2;
+  s.omb2 = (float)__dsub_rn(1.0, hp.beta2);
+  s.bc2_sqrt = (float)__dsqrt_rn(bc2);  // bias_correction2 ** 0.5
+  s.neg_step_size = (float)(-__ddiv_rn(hp.lr, bc1));
+  s.eps = (float)hp.eps;
+}
+
+__device__ __forceinline__ void adamw_elem(const ChunkScalars& s, float g, float& w, float& m,
+                                           float& v) {
+  w = __fmul_rn(w, s.decay);
+  const float diff = __fsub_rn(g, m);
+  m = s.small_w1 ? __fmaf_rn(s.w1, diff, m) : __fmaf_rn(s.w1m1, diff, g);
+  v = __fmaf_rn(__fmul_rn(s.omb2, g), g, __fmul_rn(v, s.beta2));
+  const float d = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), s.bc2_sqrt), s.eps);
+  w = __fadd_rn(w, __fdiv_rn(__fmul_rn(s.neg_step_size, m), d));
+}
+
+__device__ __forceinline__ float clip_coefficient(float norm, float max_norm) {
+  // clip_grad.py:165-169: clamp(max_norm / (norm + 1e-6), max=1); python_float / tensor is
+  // tensor.reciprocal() * python_float; clamp keeps NaN.
+  const float t = __fadd_rn(norm, 1e-6f);
+  const float c = __fmul_rn(__frcp_rn(t), max_norm);
+  return c > 1.0f ? 1.0f : c;
+}
+
+template <class G, bool BF16_PARAM, int U>
+__global__ void __launch_bounds__(kThreads)
+adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
+             const b2o_chunk* __restrict__ chunks, int64_t n_chunks, GroupArgs groups,
+             float* __restrict__ steps, const float* __restrict__ found_inf,
+             const float* __restrict__ loss_scale, const float* __restrict__ norm_p,
+             float max_norm, float* clip_coef_out, Workspace ws) {
+  if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step: no traffic at all
+  __shared__ ChunkScalars sc;
+  __shared__ int is_last;
+  const float inv = inv_scale_of(loss_scale);
+  const float coef = norm_p ? clip_coefficient(*norm_p, max_norm) : 1.0f;
+  if (clip_coef_out && blockIdx.x == 0 && threadIdx.x == 0) *clip_coef_out = coef;
+
+  for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const b2o_chunk ch = chunks[c];
+    const b2o_tensor& t = tensors[ch.tensor];
+    __syncthreads();  // previous chunk's readers of `sc` are done
+    if (threadIdx.x == 0) chunk_scalars(groups.g[t.group], steps[t.slot], sc);
+    __syncthreads();
+    const ChunkScalars s = sc;
+    const void* gp = t.grad;
+    float* wp = t.master;
+    float* mp = t.exp_avg;
+    float* vp = t.exp_avg_sq;
+    uint16_t* pp = static_cast<uint16_t*>(t.param);
+    const int64_t n = ch.end - ch.begin;
+    int64_t done = 0;
+    if (t.flags & B2O_FLAG_VECTOR) {
+      const int64_t nv = n & ~int64_t(B2O_VEC - 1);
+      done = nv;
+      constexpr int64_t kStride = int64_t(kThreads) * B2O_VEC;
+      for (int64_t i0 = int64_t(threadIdx.x) * B2O_VEC; i0 < nv; i0 += kStride * U) {
+        typename G::vec_t gv[U];
+        float4 w[U][2], m[U][2], v[U][2];
+        // Issue every load of the U vectors before any arithmetic.
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * kStride;
+          if (i < nv) {
+            const int64_t e = ch.begin + i;
+            gv[u] = G::load(gp, e);
+            const float4* w4 = reinterpret_cast<const float4*>(wp + e);
+            const float4* m4 = reinterpret_cast<const float4*>(mp + e);
+            const float4* v4 = reinterpret_cast<const float4*>(vp + e);
+            w[u][0] = ld_stream(w4); w[u][1] = ld_stream(w4 + 1);
+            m[u][0] = ld_stream(m4); m[u][1] = ld_stream(m4 + 1);
+            v[u][0] = ld_stream(v4); v[u][1] = ld_stream(v4 + 1);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * kStride;
+          if (i < nv) {
+            const int64_t e = ch.begin + i;
+            float x[B2O_VEC];
+            G::unpack(gv[u], x);
+            float* wf = reinterpret_cast<float*>(w[u]);
+            float* mf = reinterpret_cast<float*>(m[u]);
+            float* vf = reinterpret_cast<float*>(v[u]);
+#pragma unroll
+            for (int k = 0; k < B2O_VEC; ++k) {
+              const float g = __fmul_rn(__fmul_rn(x[k], inv), coef);
+              adamw_elem(s, g, wf[k], mf[k], vf[k]);
+            }
+            float4* w4 = reinterpret_cast<float4*>(wp + e);
+            float4* m4 = reinterpret_cast<float4*>(mp + e);
+            float4* v4 = reinterpret_cast<float4*>(vp + e);
+            st_stream(w4, w[u][0]); st_stream(w4 + 1, w[u][1]);
+            st_stream(m4, m[u][0]); st_stream(m4 + 1, m[u][1]);
+            st_stream(v4, v[u][0]); st_stream(v4 + 1, v[u][1]);
+            if (BF16_PARAM) {
+              uint4 q;
+              q.x = pack_bf16x2(wf[0], wf[1]);
+              q.y = pack_bf16x2(wf[2], wf[3]);
+              q.z = pack_bf16x2(wf[4], wf[5]);
+              q.w = pack_bf16x2(wf[6], wf[7]);
+              st_stream(reinterpret_cast<uint4*>(pp + e), q);
+            }
+          }
+        }
+      }
+    }
+    for (int64_t i = done + threadIdx.x; i < n; i += kThreads) {
+      const int64_t e = ch.begin + i;
+      bool unused = false;
+      const float g = __fmul_rn(__fmul_rn(G::load1(gp, e, unused), inv), coef);
+      float w = wp[e], m = mp[e], v = vp[e];
+      adamw_elem(s, g, w, m, v);
+      wp[e] = w;
+      mp[e] = m;
+      vp[e] = v;
+      if (BF16_PARAM) pp[e] = to_bf16_bits(w);
+    }
+  }
+
+  // Completion ticket; the last CTA advances the step counters after every CTA has read them.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(ws.adamw_done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int ti = threadIdx.x; ti < n_tensors; ti += kThreads) {
+    const int slot = tensors[ti].slot;
+    steps[slot] = __fadd_rn(__ldcg(steps + slot), 1.0f);
+  }
+  if (threadIdx.x == 0) *ws.adamw_done = 0u;
+}
+
+template <class G, bool P>
+int launch_adamw(cudaStream_t s, const b2o_tensor* tensors, int n_tensors,
+                 const b2o_chunk* chunks, int64_t n_chunks, const GroupArgs& ga, float* steps,
+                 const float* found_inf, const float* loss_scale, const float* norm, float max_norm,
+                 float* coef_out, Workspace ws) {
+  const int grid = stream_grid((const void*)adamw_kernel<G, P, 2>, kThreads, n_chunks);
+  if (grid <= 0) return B2O_ERR_CUDA;
+  adamw_kernel<G, P, 2><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks, ga, steps,
+                                                  found_inf, loss_scale, norm, max_norm, coef_out, ws);
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}
+
+}  // namespace b2o
+
+using namespace b2o;
+
+extern "C" int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors,
+                              const b2o_chunk* chunks, int64_t n_chunks, const b2o_group* groups,
+                              int32_t n_groups, int32_t grad_dtype, int32_t param_dtype,
+                              float* steps, const float* found_inf, const float* loss_scale,
+                              const float* norm, float max_norm, float* clip_coef_out,
+                              void* workspace, void* stream) {
+  if (!tensors || !groups || !steps || !workspace || n_tensors < 0 || n_chunks < 0)
+    return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS) return B2O_ERR_ARG;
+  GroupArgs ga{};
+  for (int i = 0; i < n_groups; ++i) ga.g[i] = groups[i];
+  Workspace ws = carve_workspace(workspace, n_chunks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16p = param_dtype == B2O_BF16;
+  if (param_dtype != B2O_BF16 && param_dtype != B2O_F32) return B2O_ERR_ARG;
+  if (grad_dtype == B2O_BF16) {
+    return bf16p ? launch_adamw<GradBF16, true>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                                steps, found_inf, loss_scale, norm, max_norm,
+                                                clip_coef_out, ws)
+                 : launch_adamw<GradBF16, false>(s, tensors, n_tensors, chunks, n_chunks,
+                                                 ga, steps, found_inf, loss_scale, norm, max_norm,
+                                                 clip_coef_out, ws);
+  }
+  if (grad_dtype == B2O_F32) {
+    return bf16p ? launch_adamw<GradF32, true>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                               steps, found_inf, loss_scale, norm, max_norm,
+                                               clip_coef_out, ws)
+                 : launch_adamw<GradF32, false>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                                steps, found_inf, loss_scale, norm, max_norm,
+                                                clip_coef_out, ws);
+  }
+  return B2O_ERR_ARG;
+}

@@ -1,0 +1,165 @@
+// Pass 1 of the optimizer step: unscale + non-finite flag + L2 partial sums (sm_100a).
+//
+// Replaces, for the reference's train.py:485-486, the two gradient passes torch makes:
+//   torch._amp_foreach_non_finite_check_and_unscale_   (torch/amp/grad_scaler.py:294)
+//   torch._foreach_norm + linalg.vector_norm           (torch/nn/utils/clip_grad.py:96,106)
+// Gradients are read once (2 bytes per bf16 element) and never written; the unscale factor and
+// the clip coefficient are folded into pass 2 (b2o_adamw.cu).
+//
+// Reduction order (deterministic for a given plan and grid):
+//   element -> fp32 sum of squares over one 8-element vector (fma chain)
+//   vector  -> fp64 per-thread sum -> fixed-order CTA sum = one fp64 partial per chunk
+//   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order with a
+//              fixed lane-strided walk + xor-shuffle tree into exch[slot]
+//   slot    -> per-tensor norm fp32(sqrt(sum)), total fp32(sqrt(sum of squared norms)); the
+//              same two-level structure as clip_grad.py:_get_total_norm.
+#include <cuda_runtime.h>
+
+#include "b2o_device.cuh"
+#include "b2o_host.h"
+
+namespace b2o {
+
+// Folds n_ranks exchange vectors into found_inf / norm.  Executed by one whole CTA.
+__device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slots,
+                                  float* found_inf_out, float* norm_out, double* scratch) {
+  const int stride = n_slots + 1;
+  double local = 0.0;
+  for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
+    double sum = 0.0;
+    for (int r = 0; r < n_ranks; ++r) sum += __ldcg(exch_all + (int64_t)r * stride + s);
+    const float tn = (float)sqrt(sum);  // per-tensor norm rounded to fp32, as torch returns it
+    const double t = (double)tn;
+    local += t * t;
+  }
+  const double total_sq = block_sum(local, scratch);
+  if (threadIdx.x == 0) {
+    double bad = 0.0;
+    for (int r = 0; r < n_ranks; ++r) bad += __ldcg(exch_all + (int64_t)r * stride + n_slots);
+    if (found_inf_out) *found_inf_out = bad != 0.0 ? 1.0f : 0.0f;
+    if (norm_out) *norm_out = (float)sqrt(total_sq);
+  }
+}
+
+template <class G>
+__global__ void __launch_bounds__(kThreads)
+grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
+                  const b2o_chunk* __restrict__ chunks, int64_t n_chunks, int n_slots,
+                  const float* __restrict__ loss_scale, Workspace ws, double* exch,
+                  int flags, float* found_inf_out, float* norm_out) {
+  __shared__ double scratch[kWarps];
+  __shared__ int is_last;
+  const float inv = inv_scale_of(loss_scale);
+  bool bad = false;
+
+  for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const b2o_chunk ch = chunks[c];
+    const b2o_tensor& t = tensors[ch.tensor];
+    const void* g = t.grad;
+    double acc = 0.0;
+    const int64_t n = ch.end - ch.begin;
+    int64_t done = 0;
+    if (t.flags & B2O_FLAG_VECTOR) {
+      const int64_t nv = n & ~int64_t(B2O_VEC - 1);
+      done = nv;
+      for (int64_t i = int64_t(threadIdx.x) * B2O_VEC; i < nv; i += int64_t(kThreads) * B2O_VEC) {
+        const typename G::vec_t v = G::load(g, ch.begin + i);
+        bad |= G::nonfinite(v);
+        float x[B2O_VEC];
+        G::unpack(v, x);
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < B2O_VEC; ++k) {
+          const float u = __fmul_rn(x[k], inv);
+          s = __fmaf_rn(u, u, s);
+        }
+        acc += (double)s;
+      }
+    }
+    for (int64_t i = done + threadIdx.x; i < n; i += kThreads) {
+      const double u = (double)__fmul_rn(G::load1(g, ch.begin + i, bad), inv);
+      acc += u * u;  // exact: a squared fp32 value fits in fp64
+    }
+    const double total = block_sum(acc, scratch);
+    if (threadIdx.x == 0) ws.chunk_sums[c] = total;
+  }
+
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(ws.stats_nonfinite, 1u);
+
+  // Completion ticket: the CTA that takes the last ticket sees every partial.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(ws.stats_done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (flags & B2O_STATS_CLEAR)
+    for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
+  __syncthreads();
+  for (int ti = warp; ti < n_tensors; ti += kWarps) {
+    const b2o_tensor& t = tensors[ti];
+    double sum = 0.0;
+    for (int k = lane; k < t.chunk_count; k += 32) sum += __ldcg(ws.chunk_sums + t.chunk_begin + k);
+    sum = warp_sum(sum);
+    if (lane == 0) exch[t.slot] = sum;
+  }
+  if (threadIdx.x == 0) {
+    const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
+    if (nf) exch[n_slots] += 1.0;
+    *ws.stats_done = 0u;
+  }
+  __threadfence();
+  __syncthreads();
+  if (flags & B2O_STATS_FINALIZE)
+    finalize_norm_cta(exch, 1, n_slots, found_inf_out, norm_out, scratch);
+}
+
+__global__ void __launch_bounds__(kThreads)
+finalize_norm_kernel(const double* exch_all, int n_ranks, int n_slots, float* found_inf_out,
+                     float* norm_out) {
+  __shared__ double scratch[kWarps];
+  finalize_norm_cta(exch_all, n_ranks, n_slots, found_inf_out, norm_out, scratch);
+}
+
+}  // namespace b2o
+
+using namespace b2o;
+
+extern "C" int b2o_grad_stats(const b2o_tensor* tensors, int32_t n_tensors,
+                              const b2o_chunk* chunks, int64_t n_chunks, int32_t n_slots,
+                              int32_t grad_dtype, const float* loss_scale, void* workspace,
+                              double* exch, int32_t flags, float* found_inf_out,
+                              float* norm_out, void* stream) {
+  if (!tensors || !workspace || n_tensors < 0 || n_chunks < 0 || n_slots < 0) return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  if ((flags & B2O_STATS_FINALIZE) && (!found_inf_out || !norm_out)) return B2O_ERR_ARG;
+  Workspace ws = carve_workspace(workspace, n_chunks);
+  if (!exch) exch = ws.exch;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (grad_dtype == B2O_BF16) {
+    const int grid = stream_grid((const void*)grad_stats_kernel<GradBF16>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    grad_stats_kernel<GradBF16><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks,
+                                                          n_slots, loss_scale, ws, exch, flags,
+                                                          found_inf_out, norm_out);
+  } else if (grad_dtype == B2O_F32) {
+    const int grid = stream_grid((const void*)grad_stats_kernel<GradF32>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    grad_stats_kernel<GradF32><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks,
+                                                         n_slots, loss_scale, ws, exch, flags,
+                                                         found_inf_out, norm_out);
+  } else {
+    return B2O_ERR_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}
+
+extern "C" int b2o_finalize_norm(const double* exch_all, int32_t n_ranks, int32_t n_slots,
+                                 float* found_inf_out, float* norm_out, void* stream) {
+  if (!exch_all || n_ranks <= 0 || n_slots < 0 || !found_inf_out || !norm_out) return B2O_ERR_ARG;
+  finalize_norm_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      exch_all, n_ranks, n_slots, found_inf_out, norm_out);
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}

@@ -1,0 +1,429 @@
+"""``FusedAdamW``: a drop-in ``torch.optim.AdamW`` whose step runs as two sm_100a kernels.
+
+Drop-in site: the reference builds ``torch.optim.AdamW(build_adamw_param_groups(model, wd), lr,
+betas, eps, fused=...)`` at ``train.py:359-365`` and drives it through ``zero_grad`` (``:465``),
+``scaler.step`` (``:490``), ``state_dict`` (``checkpoint.py:41``) and ``load_state_dict``
+(``src/minigpt/optim.py:136-251``).  This class keeps that surface:
+
+* constructor arguments and defaults of ``torch.optim.AdamW`` (``torch/optim/adamw.py``), the same
+  ``param_groups`` keys (``lr, betas, eps, weight_decay, amsgrad, maximize, foreach, capturable,
+  differentiable, fused, decoupled_weight_decay``) and any extra keys the caller adds
+  (``param_names``, ``group_name``);
+* per-parameter state ``{"step", "exp_avg", "exp_avg_sq"}`` laid out as torch lays it out, plus
+  ``"master_param"`` (fp32) for bf16 parameters;
+* ``_step_supports_amp_scaling = True``: ``GradScaler.step`` hands over ``found_inf`` (and, if
+  the caller skipped ``unscale_``, ``grad_scale``) as device tensors, so no step synchronises the
+  host (``torch/amp/grad_scaler.py:418-470``).
+
+What is different underneath:
+
+* master weights, moments and step counters live in flat fp32 device buffers (one allocation
+  each, 256-byte aligned segments per parameter); the state entries are views into them;
+* ``GradScaler.unscale_`` and ``clip_grad_norm_`` of this package do not rewrite gradients; they
+  run one read-only statistics pass (``b2o_grad_stats``) and record the loss scale and clip
+  threshold, which the update kernel (``b2o_adamw_step``) applies while it updates the state --
+  so ``param.grad`` still holds the scaled gradients after ``unscale_``;
+* bf16 parameters are refreshed from the fp32 masters by the same kernel.
+
+CUDA tensors only; there is no CPU path.  Not supported (raise): ``amsgrad``, ``maximize``,
+``differentiable``, sparse gradients, fp16 parameters.
+"""
+
+from __future__ import annotations
+
+import weakref
+from collections import defaultdict
+from dataclasses import dataclass
+from itertools import chain
+from typing import Any, Iterable
+
+import numpy as np
+import torch
+
+from . import _lib
+from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
+
+_ALIGN = 64  # elements per segment alignment: 256 bytes of fp32
+
+_REGISTRY: "weakref.WeakSet[FusedAdamW]" = weakref.WeakSet()
+
+
+@dataclass
+class GradStats:
+    """Result of the statistics pass of one iteration (device tensors, no host sync)."""
+    found_inf: torch.Tensor      # 0-dim fp32, 1.0 when a gradient held inf/NaN
+    norm: torch.Tensor           # 0-dim fp32, total L2 norm of the unscaled gradients
+    loss_scale: torch.Tensor | None
+    max_norm: float | None = None
+
+
+class FusedAdamW(torch.optim.Optimizer):
+    """AdamW with decoupled weight decay, fused unscale/clip/update and bf16 param refresh."""
+
+    def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 1e-2, amsgrad: bool = False, *,
+                 maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
+                 differentiable: bool = False, fused: bool | None = None,
+                 chunk_elems: int = DEFAULT_CHUNK_ELEMS):
+        if isinstance(lr, torch.Tensor):
+            raise TypeError("FusedAdamW takes lr as a Python float")
+        if not 0.0 <= lr:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if not 0.0 <= eps:
+            raise ValueError(f"Invalid epsilon value: {eps}")
+        if not 0.0 <= betas[0] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 0: {betas[0]}")
+        if not 0.0 <= betas[1] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
+        if not 0.0 <= weight_decay:
+            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+        if amsgrad or maximize or differentiable:
+            raise NotImplementedError("FusedAdamW supports amsgrad=False, maximize=False, "
+                                      "differentiable=False only")
+        if chunk_elems <= 0 or chunk_elems % _lib.VEC:
+            raise ValueError("chunk_elems must be a positive multiple of 8")
+        defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
+                        weight_decay=weight_decay, amsgrad=False, maximize=False,
+                        foreach=foreach, capturable=capturable, differentiable=False,
+                        fused=fused, decoupled_weight_decay=True)
+        super().__init__(params, defaults)
+        self._step_supports_amp_scaling = True
+        self._chunk_elems = int(chunk_elems)
+        self._store: _FlatStore | None = None
+        self._plans: list[ChunkPlan] | None = None
+        self._plan_key: tuple | None = None
+        self._pending: GradStats | None = None
+        _REGISTRY.add(self)
+
+    # ------------------------------------------------------------------------------------
+    # torch.optim.Optimizer surface
+    # ------------------------------------------------------------------------------------
+
+    def __setstate__(self, state: dict[str, Any]) -> None:
+        super().__setstate__(state)
+        for group in self.param_groups:
+            group.setdefault("amsgrad", False)
+            group.setdefault("maximize", False)
+            group.setdefault("foreach", None)
+            group.setdefault("capturable", False)
+            group.setdefault("differentiable", False)
+            group.setdefault("fused", None)
+            group.setdefault("decoupled_weight_decay", True)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        """One AdamW update of every parameter that has a gradient.
+
+        Applies the pending unscale factor and clip coefficient recorded by this package's
+        ``GradScaler.unscale_`` / ``clip_grad_norm_`` and skips the whole update (step counters
+        included) when ``self.found_inf`` -- set by ``GradScaler.step`` -- is non-zero.
+        """
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        plans = self._prepare()
+        pend = self._pending
+        self._pending = None
+        if not plans:
+            return loss
+        store = self._store
+        device = store.device
+        found_inf = getattr(self, "found_inf", None)
+        if found_inf is not None:
+            found_inf = found_inf.to(device=device, dtype=torch.float32, non_blocking=True)
+        loss_scale = pend.loss_scale if pend is not None else None
+        grad_scale = getattr(self, "grad_scale", None)
+        if loss_scale is None and grad_scale is not None:
+            loss_scale = grad_scale.to(device=device, dtype=torch.float32, non_blocking=True)
+        norm = pend.norm if (pend is not None and pend.max_norm is not None) else None
+        max_norm = pend.max_norm if norm is not None else 0.0
+        groups = self._group_array()
+        stream = stream_ptr(device)
+        for plan in plans:
+            _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
+                      plan.n_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
+                      plan.param_dtype, store.steps.data_ptr(),
+                      None if found_inf is None else found_inf.data_ptr(),
+                      None if loss_scale is None else loss_scale.data_ptr(),
+                      None if norm is None else norm.data_ptr(), float(max_norm), None,
+                      plan.workspace.data_ptr(), stream)
+        return loss
+
+    def state_dict(self) -> dict[str, Any]:
+        self._sync_state()
+        return super().state_dict()
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        """Load a ``state_dict`` of this class or of ``torch.optim.AdamW``.
+
+        Unlike ``torch.optim.Optimizer.load_state_dict`` (``torch/optim/optimizer.py``), state
+        tensors are not cast to the parameter dtype: moments and masters stay fp32 under bf16
+        parameters.  A state without ``master_param`` (a reference checkpoint of fp32
+        parameters) initialises the master from the parameter.
+        """
+        state_dict = state_dict.copy()
+        for pre_hook in self._optimizer_load_state_dict_pre_hooks.values():
+            res = pre_hook(self, state_dict)
+            if res is not None:
+                state_dict = res
+        groups = self.param_groups
+        saved_groups = [dict(g) for g in state_dict["param_groups"]]
+        if len(groups) != len(saved_groups):
+            raise ValueError("loaded state dict has a different number of parameter groups")
+        if any(len(g["params"]) != len(s["params"]) for g, s in zip(groups, saved_groups)):
+            raise ValueError("loaded state dict contains a parameter group that doesn't match "
+                             "the size of optimizer's group")
+        id_map = dict(zip(chain.from_iterable(g["params"] for g in saved_groups),
+                          chain.from_iterable(g["params"] for g in groups)))
+        new_groups = []
+        for g, s in zip(groups, saved_groups):
+            s["params"] = g["params"]
+            if "param_names" in g and "param_names" not in s:
+                s["param_names"] = g["param_names"]
+            new_groups.append(s)
+        foreign = {}
+        state: defaultdict = defaultdict(dict)
+        for k, v in state_dict["state"].items():
+            if k in id_map:
+                state[id_map[k]] = dict(v)
+            else:
+                foreign[k] = v
+        self.__setstate__({"state": state, "param_groups": new_groups})
+        self.state.update(foreign)
+        self._plans = None
+        self._plan_key = None
+        self._sync_state(force=True)
+        for post_hook in self._optimizer_load_state_dict_post_hooks.values():
+            post_hook(self)
+
+    # ------------------------------------------------------------------------------------
+    # Hooks used by GradScaler / clip_grad_norm_ of this package
+    # ------------------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def _grad_stats(self, loss_scale: torch.Tensor | None) -> GradStats:
+        """Run the read-only statistics pass over the current gradients (no host sync)."""
+        plans = self._prepare()
+        store = self._store
+        device = store.device if store is not None else torch.device("cuda",
+                                                                     torch.cuda.current_device())
+        out = torch.zeros(2, dtype=torch.float32, device=device)
+        if plans:
+            stream = stream_ptr(device)
+            ls = None
+            if loss_scale is not None:
+                loss_scale = loss_scale.to(device=device, dtype=torch.float32)
+                ls = loss_scale.data_ptr()
+            single = len(plans) == 1
+            for k, plan in enumerate(plans):
+                flags = (_lib.STATS_CLEAR if k == 0 else 0) | \
+                    (_lib.STATS_FINALIZE if single else 0)
+                _lib.call("b2o_grad_stats", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
+                          plan.n_chunks, store.n_slots, plan.grad_dtype, ls,
+                          plan.workspace.data_ptr(), store.exch.data_ptr(), flags,
+                          out.data_ptr(), out.data_ptr() + 4, stream)
+            if not single:
+                _lib.call("b2o_finalize_norm", store.exch.data_ptr(), 1, store.n_slots,
+                          out.data_ptr(), out.data_ptr() + 4, stream)
+        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale)
+        return self._pending
+
+    def _owns_exactly(self, params: list[torch.Tensor]) -> bool:
+        mine = {id(p) for g in self.param_groups for p in g["params"] if p.grad is not None}
+        theirs = {id(p) for p in params if p.grad is not None}
+        return mine == theirs
+
+    def set_master_(self, param: torch.Tensor, master: torch.Tensor) -> None:
+        """Overwrite the fp32 master (and the bf16 copy) of one parameter, e.g. from fp32
+        weights that a bf16 model cannot hold."""
+        self._sync_state()
+        store = self._store
+        slot = next((i for i, q in enumerate(store.params) if q is param), None)
+        if slot is None:
+            raise KeyError("parameter is not managed by this optimizer")
+        own = store.views[slot]
+        with torch.no_grad():
+            if "master_param" in own:
+                own["master_param"].copy_(master.reshape(param.shape))
+                param.copy_(own["master_param"])
+            else:
+                param.copy_(master.reshape(param.shape))
+
+    # ------------------------------------------------------------------------------------
+    # internals
+    # ------------------------------------------------------------------------------------
+
+    def _group_array(self) -> np.ndarray:
+        n = len(self.param_groups)
+        if n > _lib.MAX_GROUPS:
+            raise ValueError(f"at most {_lib.MAX_GROUPS} param groups are supported")
+        arr = np.zeros(n, dtype=_lib.GROUP_DTYPE)
+        for i, g in enumerate(self.param_groups):
+            lr = g["lr"]
+            if isinstance(lr, torch.Tensor):
+                lr = float(lr)
+            b1, b2 = g["betas"]
+            arr[i] = (float(lr), float(b1), float(b2), float(g["eps"]), float(g["weight_decay"]))
+        return arr
+
+    def _all_params(self) -> list[torch.Tensor]:
+        return [p for g in self.param_groups for p in g["params"]]
+
+    def _ensure_store(self) -> "_FlatStore":
+        if self._store is None:
+            self._store = _FlatStore(self._all_params())
+        return self._store
+
+    def _sync_state(self, force: bool = False) -> None:
+        """Make every ``self.state[p]`` entry a view into the flat buffers.
+
+        Entries written from outside (``load_state_dict`` above, or a loader that assigns
+        ``optimizer.state[p] = {...}`` such as the reference's ``optim.py:242-251``) are copied
+        into the flat buffers with their values cast to fp32.
+        """
+        if not self._all_params():
+            return
+        store = self._ensure_store()
+        for slot, p in enumerate(store.params):
+            cur = self.state.get(p)
+            own = store.views[slot]
+            if cur is own:
+                continue
+            if cur:
+                store.ingest(slot, cur)
+                self.state[p] = own
+            elif force:
+                self.state.pop(p, None)
+
+    def _prepare(self) -> list[ChunkPlan] | None:
+        """Refresh state views and the device plans; returns None when no grads exist."""
+        params = self._all_params()
+        if not params:
+            return None
+        store = self._ensure_store()
+        self._sync_state()
+        active = []
+        for slot, p in enumerate(store.params):
+            g = p.grad
+            if g is None:
+                continue
+            if g.is_sparse:
+                raise RuntimeError("FusedAdamW does not support sparse gradients")
+            active.append((slot, p, g))
+        if not active:
+            return None
+        key = tuple((slot, g.data_ptr(), p.data_ptr(), g.dtype) for slot, p, g in active)
+        if key != self._plan_key:
+            self._plans = self._build_plans(active)
+            self._plan_key = key
+        for slot, p, _ in active:
+            if p not in self.state or self.state[p] is not store.views[slot]:
+                self.state[p] = store.views[slot]
+        return self._plans
+
+    def _build_plans(self, active) -> list[ChunkPlan]:
+        store = self._store
+        gid = {}
+        for gi, g in enumerate(self.param_groups):
+            for p in g["params"]:
+                gid[id(p)] = gi
+        buckets: dict[tuple[int, int], list[Entry]] = {}
+        for slot, p, g in active:
+            if g.device != store.device or p.device != store.device:
+                raise RuntimeError("FusedAdamW needs every parameter and gradient on one CUDA "
+                                   "device")
+            if g.shape != p.shape:
+                raise RuntimeError("gradient shape does not match its parameter")
+            if not g.is_contiguous() or not p.is_contiguous():
+                raise RuntimeError("FusedAdamW needs contiguous parameters and gradients")
+            gd, pd = dtype_code(g.dtype), dtype_code(p.dtype)
+            off, n = store.offsets[slot], p.numel()
+            master = store.master_ptr(slot)
+            entry = Entry(grad=g.data_ptr(), param=p.data_ptr() if pd == _lib.BF16 else 0,
+                          master=master, exp_avg=store.exp_avg.data_ptr() + 4 * off,
+                          exp_avg_sq=store.exp_avg_sq.data_ptr() + 4 * off, numel=n,
+                          group=gid[id(p)], slot=slot)
+            buckets.setdefault((gd, pd), []).append(entry)
+        plans = []
+        for (gd, pd), entries in buckets.items():
+            plans.append(ChunkPlan(store.device, entries, len(self.param_groups), store.n_slots,
+                                   gd, pd, self._chunk_elems))
+        return plans
+
+
+class _FlatStore:
+    """Flat fp32 device buffers holding every parameter's optimizer state."""
+
+    def __init__(self, params: list[torch.Tensor]):
+        devs = {p.device for p in params}
+        if len(devs) != 1 or next(iter(devs)).type != "cuda":
+            raise RuntimeError("FusedAdamW needs every parameter on one CUDA device "
+                               f"(got {sorted(map(str, devs))}); there is no CPU path")
+        self.device = next(iter(devs))
+        for p in params:
+            if p.dtype not in (torch.bfloat16, torch.float32):
+                raise TypeError(f"unsupported parameter dtype {p.dtype} (bf16 or fp32 only)")
+        self.params = params
+        self.n_slots = len(params)
+        self.offsets = []
+        self.master_offsets = []
+        total = 0
+        mtotal = 0
+        for p in params:
+            self.offsets.append(total)
+            total += _round_up(p.numel(), _ALIGN)
+            if p.dtype == torch.bfloat16:
+                self.master_offsets.append(mtotal)
+                mtotal += _round_up(p.numel(), _ALIGN)
+            else:
+                self.master_offsets.append(-1)
+        with torch.no_grad():
+            self.exp_avg = torch.zeros(max(total, 1), dtype=torch.float32, device=self.device)
+            self.exp_avg_sq = torch.zeros(max(total, 1), dtype=torch.float32, device=self.device)
+            self.master = torch.zeros(max(mtotal, 1), dtype=torch.float32, device=self.device)
+            self.steps = torch.zeros(max(self.n_slots, 1), dtype=torch.float32, device=self.device)
+            self.exch = torch.zeros(self.n_slots + 1, dtype=torch.float64, device=self.device)
+            self.views = []
+            for slot, p in enumerate(params):
+                off, n = self.offsets[slot], p.numel()
+                v = {"step": self.steps[slot],
+                     "exp_avg": self.exp_avg[off:off + n].view(p.shape),
+                     "exp_avg_sq": self.exp_avg_sq[off:off + n].view(p.shape)}
+                if self.master_offsets[slot] >= 0:
+                    mo = self.master_offsets[slot]
+                    mv = self.master[mo:mo + n].view(p.shape)
+                    mv.copy_(p.detach())
+                    v["master_param"] = mv
+                self.views.append(v)
+
+    def master_ptr(self, slot: int) -> int:
+        mo = self.master_offsets[slot]
+        if mo < 0:
+            return self.params[slot].data_ptr()
+        return self.master.data_ptr() + 4 * mo
+
+    @torch.no_grad()
+    def ingest(self, slot: int, st: dict) -> None:
+        own = self.views[slot]
+        p = self.params[slot]
+        if "step" in st:
+            val = st["step"]
+            own["step"].fill_(float(val.item() if isinstance(val, torch.Tensor) else val))
+        for k in ("exp_avg", "exp_avg_sq"):
+            if k in st:
+                own[k].copy_(st[k].reshape(p.shape))
+        if "master_param" in own:
+            if "master_param" in st:
+                own["master_param"].copy_(st["master_param"].reshape(p.shape))
+                p.copy_(own["master_param"])
+            else:
+                own["master_param"].copy_(p)
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def fused_optimizers() -> list[FusedAdamW]:
+    return list(_REGISTRY)
