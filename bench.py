@@ -39,7 +39,7 @@ STATS_BYTES = 2    # read g
 FALLBACK_HBM_GBS = 6650.0
 LR, BETAS, EPS, WD, CLIP = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
 SCALES = {"qwen3_8b": 2.0 ** 15}
-GRAD_STD = {"flat_2_28": 1e-2}
+GRAD_STD = {"flat_2_28": 1e-2, "flat_2_26": 1e-2}
 
 
 def log(*a):

@@ -12,7 +12,8 @@ decay split (group 0 = ``ndim >= 2`` with weight decay, group 1 = the rest), exa
   2048, MLP 6144, 16 q / 8 kv heads of 128, vocab 151936, tied: 310 tensors, 1,720,574,976;
 * ``qwen3_8b`` -- 36 layers, hidden 4096, MLP 12288, 32 q / 8 kv heads of 128, untied
   ``lm_head``: 399 tensors, 8,190,735,360 params;
-* ``flat_2_28`` -- one tensor of 2**28 elements.
+* ``flat_2_28`` -- one tensor of 2**28 elements; ``flat_2_26`` -- 2**26 elements, the small case
+  used for profiler captures (about 1.2 GB on the device, still far above the L2).
 
 The lists are written out here (the benchmark box has no reference checkout); a CPU test checks
 them against ``tests/golden/param_shapes.json``, which was generated from the reference classes.
@@ -71,6 +72,7 @@ WORKLOADS = {
     "qwen3_1_7b": lambda: qwen3(151936, 2048, 6144, 28, 16, 8, 128, True),
     "qwen3_8b": lambda: qwen3(151936, 4096, 12288, 36, 32, 8, 128, False),
     "flat_2_28": lambda: [("flat", (1 << 28,), 0)],
+    "flat_2_26": lambda: [("flat", (1 << 26,), 0)],
 }
 
 
