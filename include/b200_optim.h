@@ -41,7 +41,8 @@ typedef enum {
   B2O_ERR_CAPACITY = -2,  /* an output array is too small for the plan                      */
   B2O_ERR_LAUNCH = -3,    /* the kernel launch failed (cudaGetLastError)                    */
   B2O_ERR_CUDA = -4,      /* another CUDA runtime call failed                               */
-  B2O_ERR_TABLE = -5      /* a tensor table entry is inconsistent (overlap, bad slot/group) */
+  B2O_ERR_TABLE = -5,     /* a tensor table entry is inconsistent (overlap, bad slot/group) */
+  B2O_ERR_TOO_LARGE = -6  /* the plan exceeds the fixed scratch of b2o_grad_stats_noalloc    */
 } b2o_status;
 
 typedef enum { B2O_BF16 = 0, B2O_F32 = 1 } b2o_dtype;
@@ -141,6 +142,31 @@ int b2o_grad_stats(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk
                    int64_t n_chunks, int32_t n_slots, int32_t grad_dtype,
                    const float* loss_scale, void* workspace, double* exch, int32_t flags,
                    float* found_inf_out, float* norm_out, void* stream);
+
+/* Allocation-free variant of b2o_grad_stats, for callers that cannot allocate device memory:
+ * an FFI host that only holds pointers handed to it by another runtime and has no allocator to
+ * give this library, or a training process already at its memory ceiling where one more
+ * allocation would fail.  No counterpart in the reference (torch allocates its own scratch).
+ *
+ * Same pass and same results as b2o_grad_stats called with
+ * B2O_STATS_CLEAR | B2O_STATS_FINALIZE, but the scratch (completion counters, one double per
+ * chunk, n_slots + 1 per-slot sums) lives in one fixed array inside this library instead of a
+ * caller workspace.  That array holds B2O_NOALLOC_MAX_CHUNKS chunks and B2O_NOALLOC_MAX_SLOTS
+ * slots (about 288 KiB); every GPU that loads the library keeps it until the process exits.
+ * Larger plans are rejected with B2O_ERR_TOO_LARGE -- use a larger chunk_elems or
+ * b2o_grad_stats.  The call allocates and frees nothing.
+ *
+ * The first call on a device (with that device current) looks up the array's device address
+ * once (cudaGetSymbolAddress); make that first call before any stream capture.  Each call
+ * clears the counters on `stream` before its kernel.  All calls share the one array and it keeps
+ * the last call's contents, so calls whose kernels overlap on the GPU (different streams without
+ * ordering, or different threads) race and give wrong results: order them on one stream. */
+#define B2O_NOALLOC_MAX_CHUNKS 32768
+#define B2O_NOALLOC_MAX_SLOTS 4096
+int b2o_grad_stats_noalloc(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk* chunks,
+                           int64_t n_chunks, int32_t n_slots, int32_t grad_dtype,
+                           const float* loss_scale, float* found_inf_out, float* norm_out,
+                           void* stream);
 
 /* Fold `n_ranks` exchange vectors (laid out rank-major, n_slots+1 doubles each) in rank order:
  * per-slot norm = fp32(sqrt(sum)), total = fp32(sqrt(sum of squared per-slot norms)), and

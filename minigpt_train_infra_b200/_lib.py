@@ -26,6 +26,10 @@ STATS_CLEAR = 2
 
 FLAG_VECTOR = 1
 
+NOALLOC_MAX_CHUNKS = 32768
+NOALLOC_MAX_SLOTS = 4096
+ERR_TOO_LARGE = -6
+
 # Host mirrors of the C structs (same field order, sizes and alignment as b200_optim.h).
 TENSOR_DTYPE = np.dtype([
     ("grad", "<u8"), ("param", "<u8"), ("master", "<u8"), ("exp_avg", "<u8"),
@@ -61,6 +65,7 @@ SIGNATURES = {
     "b2o_workspace_init": (ctypes.c_int, [_P, ctypes.c_size_t, _P]),
     "b2o_grad_stats": (ctypes.c_int, [_P, _I32, _P, _I64, _I32, _I32, _P, _P, _P, _I32, _P, _P,
                                       _P]),
+    "b2o_grad_stats_noalloc": (ctypes.c_int, [_P, _I32, _P, _I64, _I32, _I32, _P, _P, _P, _P]),
     "b2o_finalize_norm": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _P]),
     "b2o_adamw_step": (ctypes.c_int, [_P, _I32, _P, _I64, _P, _I32, _I32, _I32, _P, _P, _P, _P,
                                       _F32, _P, _P, _P]),

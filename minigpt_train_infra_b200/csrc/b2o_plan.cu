@@ -55,6 +55,8 @@ extern "C" const char* b2o_status_string(int status) {
     case B2O_ERR_LAUNCH: return "kernel launch failed";
     case B2O_ERR_CUDA: return "CUDA runtime call failed";
     case B2O_ERR_TABLE: return "inconsistent tensor table";
+    case B2O_ERR_TOO_LARGE:
+      return "plan exceeds the fixed scratch of b2o_grad_stats_noalloc (too many chunks or slots)";
     default: return "unknown status";
   }
 }

@@ -15,6 +15,8 @@
 //              same two-level structure as clip_grad.py:_get_total_norm.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "b2o_device.cuh"
 #include "b2o_host.h"
 
@@ -161,5 +163,75 @@ extern "C" int b2o_finalize_norm(const double* exch_all, int32_t n_ranks, int32_
   if (!exch_all || n_ranks <= 0 || n_slots < 0 || !found_inf_out || !norm_out) return B2O_ERR_ARG;
   finalize_norm_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       exch_all, n_ranks, n_slots, found_inf_out, norm_out);
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free variant (b2o_grad_stats_noalloc).  Some hosts cannot allocate device memory
+// for the statistics scratch -- an FFI caller that only holds pointers another runtime handed it,
+// or a process at its memory ceiling -- so this entry point keeps its scratch in one fixed array
+// of this library and launches the same kernel as b2o_grad_stats over it.
+// ---------------------------------------------------------------------------------------------
+
+namespace b2o {
+
+constexpr size_t kNoallocScratchBytes =
+    (64 + sizeof(double) * (size_t(B2O_NOALLOC_MAX_CHUNKS) + B2O_NOALLOC_MAX_SLOTS + 1) + 255) /
+    256 * 256;
+
+// The fixed scratch: completion counters, per-chunk partials and per-slot sums, laid out as
+// carve_workspace() expects.  Host code must not take its address directly; the device address
+// comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device on that device's first call.
+static void* noalloc_scratch_ptr(int device) {
+  static std::mutex mu;
+  static void* cached[64] = {nullptr};
+  if (device < 0 || device >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[device] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    cached[device] = p;
+  }
+  return cached[device];
+}
+
+}  // namespace b2o
+
+extern "C" int b2o_grad_stats_noalloc(const b2o_tensor* tensors, int32_t n_tensors,
+                                      const b2o_chunk* chunks, int64_t n_chunks,
+                                      int32_t n_slots, int32_t grad_dtype,
+                                      const float* loss_scale, float* found_inf_out,
+                                      float* norm_out, void* stream) {
+  if (!tensors || n_tensors < 0 || n_chunks < 0 || n_slots < 0 || !found_inf_out || !norm_out)
+    return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  if (grad_dtype != B2O_BF16 && grad_dtype != B2O_F32) return B2O_ERR_ARG;
+  if (n_chunks > B2O_NOALLOC_MAX_CHUNKS || n_slots > B2O_NOALLOC_MAX_SLOTS)
+    return B2O_ERR_TOO_LARGE;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return B2O_ERR_CUDA;
+  void* scratch = noalloc_scratch_ptr(device);
+  if (scratch == nullptr) return B2O_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The counters must start at zero; the partial sums are written before they are read.
+  if (cudaMemsetAsync(scratch, 0, ws_counter_bytes(), s) != cudaSuccess) return B2O_ERR_CUDA;
+  Workspace ws = carve_workspace(scratch, n_chunks);
+  const int flags = B2O_STATS_CLEAR | B2O_STATS_FINALIZE;
+  if (grad_dtype == B2O_BF16) {
+    const int grid = stream_grid((const void*)grad_stats_kernel<GradBF16>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    grad_stats_kernel<GradBF16><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks,
+                                                          n_slots, loss_scale, ws, ws.exch, flags,
+                                                          found_inf_out, norm_out);
+  } else {
+    const int grid = stream_grid((const void*)grad_stats_kernel<GradF32>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    grad_stats_kernel<GradF32><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks,
+                                                         n_slots, loss_scale, ws, ws.exch, flags,
+                                                         found_inf_out, norm_out);
+  }
   return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
 }
