@@ -268,18 +268,25 @@ def run_ours(args) -> None:
     groups = [g for g in groups if g["params"]]
     if ws > 1:
         from minigpt_train_infra_b200 import ZeroAdamW
-        opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=pg)
-        opt.seed_state_(master_std=0.02, m_std=1e-3, v_scale=1e-6, step=999.0)
-        grads = opt.make_flat_grads_()
+        opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=pg,
+                        defer_param_gather=True)
+        fill_seeded(opt.master, 1 + 101 * rank, 0.02)
+        fill_seeded(opt.exp_avg, 2 + 101 * rank, 1e-3)
+        fill_seeded(opt.exp_avg_sq, 3 + 101 * rank, 1e-6, absval=True)
+        opt.steps.fill_(999.0)
+        with torch.no_grad():
+            opt.owned_param_shard().copy_(opt.master)
+        opt.gather_params()
         fill_seeded(opt.flat_grad, 7, std * scale)
-        scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
+        grads = opt.make_flat_grads_()
         step_params = opt.managed_params()
+        params = step_params
     else:
         opt = FusedAdamW(groups, lr=LR, betas=BETAS, eps=EPS)
         seed_state(opt, params)
         grads = make_grads(params, scale, std)
-        scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
         step_params = params
+    scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
     for p, g in zip(params, grads):
         p.grad = g
     scaler.scale(torch.ones((), device=device))  # creates the scale tensor, as loss scaling does
@@ -325,6 +332,9 @@ def run_ours(args) -> None:
         total_ms, stats_ms, adamw_ms, upd_ms = [float(x) for x in t.tolist()]
     ms_per_step = total_ms / args.steps
     value = P * args.steps / (total_ms / 1e3) / 1e9
+    allgather = None
+    if ws > 1:
+        allgather = time_allgather(args, opt, one_step, device, P, ws)
     P_local = opt.local_numel() if ws > 1 else P
     peak, peak_kind = hbm_peak()
     achieved = ADAMW_BYTES * P_local / (adamw_ms / 1e3) / 1e9
@@ -377,11 +387,45 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
         }
         if ws > 1:
-            line["allgather"] = getattr(opt, "last_allgather_report", None)
+            line["allgather"] = allgather
         print(json.dumps(line), flush=True)
     if pg is not None:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def time_allgather(args, opt, one_step, device, P, ws):
+    """The bf16 parameter all-gather of ZeRO-1, timed on its own and after each update."""
+    import torch.distributed as dist
+    k = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev[0].record()
+    for _ in range(k):
+        opt.gather_params()
+    ev[1].record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev[2].record()
+    for _ in range(k):
+        one_step()
+        opt.gather_params()
+    ev[3].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ag_ms, full_ms = (float(x) / k for x in t.tolist())
+    recv = 2 * opt.geom.padded * (ws - 1) / ws  # bytes each rank receives per gather
+    return {"ms": round(ag_ms, 4), "recv_bytes_per_rank": int(recv),
+            "gbs_per_rank": round(recv / (ag_ms / 1e3) / 1e9, 1),
+            "nvlink_peak_gbs": 770.0,
+            "frac_of_nvlink": round(recv / (ag_ms / 1e3) / 1e9 / 770.0, 4),
+            "full_step_ms": round(full_ms, 4),
+            "full_step_gparams_s": round(P / (full_ms / 1e3) / 1e9, 3),
+            "note": "in-place NCCL all_gather_into_tensor of the bf16 shards; value above times "
+                    "the sharded update (stats + norm-partial exchange + AdamW + scaler update), "
+                    "full_step_* times update + this gather back to back"}
 
 
 def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
@@ -389,11 +433,16 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
     and the step's result (norm, found_inf, scale) read back to the host each step."""
     from minigpt_train_infra_b200 import clip_grad_norm_
     steps = max(2, min(args.steps, args.e2e_steps))
+    if pg is not None:
+        # under ZeRO-1 a rank's step consumes only the gradients of its own shard
+        grads = [opt.flat_grad[opt.geom.lo:opt.geom.hi]]
     host = [torch.empty(g.shape, dtype=g.dtype, pin_memory=True) for g in grads]
     for h, g in zip(host, grads):
         h.copy_(g)
     res_host = torch.empty(3, dtype=torch.float32, pin_memory=True)
     h2d = sum(g.numel() * g.element_size() for g in grads)
+    if pg is not None:
+        h2d *= torch.distributed.get_world_size()
 
     def step():
         for g, h in zip(grads, host):
@@ -425,7 +474,9 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
         ms = float(t.item())
     del host
     return {"value": round(P * steps / (ms / 1e3) / 1e9, 3), "unit": "Gparams/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12, "steps": steps,
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": 12 * (torch.distributed.get_world_size() if pg else 1),
+            "steps": steps,
             "ms_per_step": round(ms / steps, 3)}
 
 

@@ -6,7 +6,8 @@ Drop-in site: ``train.py:366-370`` (construction), ``:479`` (``scale``), ``:485`
 the three methods below is inherited unchanged, so ``state_dict`` keeps torch's five keys
 (``scale, growth_factor, backoff_factor, growth_interval, _growth_tracker``).
 
-For a :class:`~minigpt_train_infra_b200.optim.FusedAdamW`:
+For a :class:`~minigpt_train_infra_b200.optim.FusedAdamW` or
+:class:`~minigpt_train_infra_b200.zero1.ZeroAdamW`:
 
 * ``unscale_`` runs the read-only statistics pass (``b2o_grad_stats``): the non-finite flag and
   the L2 norm of the unscaled gradients, in one read of the gradients.  It does not rewrite
@@ -28,13 +29,13 @@ import torch
 from torch.amp.grad_scaler import OptState, _refresh_per_optimizer_state
 
 from . import _lib
-from .optim import FusedAdamW
+from .optim import is_fused
 from .plan import stream_ptr
 
 
 class GradScaler(torch.amp.GradScaler):
     def unscale_(self, optimizer: torch.optim.Optimizer) -> None:
-        if not isinstance(optimizer, FusedAdamW):
+        if not is_fused(optimizer):
             return super().unscale_(optimizer)
         if not self._enabled:
             return
@@ -50,7 +51,7 @@ class GradScaler(torch.amp.GradScaler):
         optimizer_state["stage"] = OptState.UNSCALED
 
     def step(self, optimizer: torch.optim.Optimizer, *args: Any, **kwargs: Any):
-        if not isinstance(optimizer, FusedAdamW):
+        if not is_fused(optimizer):
             return super().step(optimizer, *args, **kwargs)
         if not self._enabled:
             return optimizer.step(*args, **kwargs)

@@ -4,7 +4,8 @@ Drop-in site: ``train.py:486`` calls ``torch.nn.utils.clip_grad_norm_(model.para
 grad_clip)`` and keeps the returned norm as a device tensor (``:487-489``).
 
 When the parameters are exactly the (gradient-carrying) parameters of one
-:class:`~minigpt_train_infra_b200.optim.FusedAdamW`, this returns the total norm the statistics
+:class:`~minigpt_train_infra_b200.optim.FusedAdamW` (or of one ``ZeroAdamW``, where the norm is
+the global one over all ranks), this returns the total norm the statistics
 pass computed (running that pass now if ``GradScaler.unscale_`` did not) and records
 ``max_norm``; the update kernel then multiplies by ``clamp(max_norm / (norm + 1e-6), max=1)``
 (``torch/nn/utils/clip_grad.py:165-174``) while it updates the state.  Gradients are not
@@ -17,7 +18,7 @@ from typing import Iterable
 
 import torch
 
-from .optim import FusedAdamW, fused_optimizers
+from .optim import fused_optimizers
 
 
 def clip_grad_norm_(parameters: torch.Tensor | Iterable[torch.Tensor], max_norm: float,

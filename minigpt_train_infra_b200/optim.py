@@ -45,7 +45,7 @@ from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
 
 _ALIGN = 64  # elements per segment alignment: 256 bytes of fp32
 
-_REGISTRY: "weakref.WeakSet[FusedAdamW]" = weakref.WeakSet()
+_REGISTRY: weakref.WeakSet = weakref.WeakSet()
 
 
 @dataclass
@@ -57,31 +57,40 @@ class GradStats:
     max_norm: float | None = None
 
 
+def validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
+                        chunk_elems) -> None:
+    """torch.optim.Adam's argument checks (torch/optim/adam.py:51-86) plus this package's limits."""
+    if isinstance(lr, torch.Tensor):
+        raise TypeError("the fused optimizers take lr as a Python float")
+    if not 0.0 <= lr:
+        raise ValueError(f"Invalid learning rate: {lr}")
+    if not 0.0 <= eps:
+        raise ValueError(f"Invalid epsilon value: {eps}")
+    if not 0.0 <= betas[0] < 1.0:
+        raise ValueError(f"Invalid beta parameter at index 0: {betas[0]}")
+    if not 0.0 <= betas[1] < 1.0:
+        raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
+    if not 0.0 <= weight_decay:
+        raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+    if amsgrad or maximize or differentiable:
+        raise NotImplementedError("the fused optimizers support amsgrad=False, maximize=False, "
+                                  "differentiable=False only")
+    if chunk_elems <= 0 or chunk_elems % _lib.VEC:
+        raise ValueError("chunk_elems must be a positive multiple of 8")
+
+
 class FusedAdamW(torch.optim.Optimizer):
     """AdamW with decoupled weight decay, fused unscale/clip/update and bf16 param refresh."""
+
+    _b2o_fused = True
 
     def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 1e-2, amsgrad: bool = False, *,
                  maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
                  differentiable: bool = False, fused: bool | None = None,
                  chunk_elems: int = DEFAULT_CHUNK_ELEMS):
-        if isinstance(lr, torch.Tensor):
-            raise TypeError("FusedAdamW takes lr as a Python float")
-        if not 0.0 <= lr:
-            raise ValueError(f"Invalid learning rate: {lr}")
-        if not 0.0 <= eps:
-            raise ValueError(f"Invalid epsilon value: {eps}")
-        if not 0.0 <= betas[0] < 1.0:
-            raise ValueError(f"Invalid beta parameter at index 0: {betas[0]}")
-        if not 0.0 <= betas[1] < 1.0:
-            raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
-        if not 0.0 <= weight_decay:
-            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
-        if amsgrad or maximize or differentiable:
-            raise NotImplementedError("FusedAdamW supports amsgrad=False, maximize=False, "
-                                      "differentiable=False only")
-        if chunk_elems <= 0 or chunk_elems % _lib.VEC:
-            raise ValueError("chunk_elems must be a positive multiple of 8")
+        validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
+                            chunk_elems)
         defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
                         weight_decay=weight_decay, amsgrad=False, maximize=False,
                         foreach=foreach, capturable=capturable, differentiable=False,
@@ -425,5 +434,10 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
-def fused_optimizers() -> list[FusedAdamW]:
+def fused_optimizers() -> list:
+    """Live optimizers of this package (FusedAdamW and ZeroAdamW instances)."""
     return list(_REGISTRY)
+
+
+def is_fused(optimizer) -> bool:
+    return bool(getattr(optimizer, "_b2o_fused", False))

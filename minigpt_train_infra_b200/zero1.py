@@ -1,0 +1,341 @@
+"""``ZeroAdamW``: the fused AdamW step with ZeRO-1 sharding over the GPUs of one node.
+
+No counterpart in the reference: its training loop is single-device (``train.py``) and its only
+process-group code serves tensor-parallel inference (``src/minigpt/distributed.py:46-148``).  This
+optimizer reuses that boundary's choice -- ``torch.distributed`` with NCCL, one process per GPU --
+and the step kernels of this package:
+
+* Layout.  Every parameter becomes a view into one flat buffer (``flat_param``), its gradient a
+  view into a second one (``flat_grad``); each parameter's segment starts on a 64-element
+  boundary and the total is padded to a multiple of ``64 * world_size``.  Rank ``r`` owns the
+  contiguous range ``[r*S, (r+1)*S)`` with ``S = padded_total / world_size`` and keeps fp32
+  master, ``exp_avg`` and ``exp_avg_sq`` for that range only (12 bytes per owned element).
+* Step.  (1) the statistics pass over the owned gradient range writes one fp64 sum of squares
+  per parameter slot plus a non-finite flag; (2) an NCCL all-gather of those ``n_slots + 1``
+  doubles from every rank; (3) a one-CTA kernel sums them in rank order (the same total on
+  every rank, independent of NCCL's reduction order) into the norm and ``found_inf``; (4) the
+  AdamW kernel updates the owned range and writes its bf16 parameters; (5) an in-place NCCL
+  all-gather of the bf16 shards refreshes ``flat_param`` on every rank.
+* Skips.  ``found_inf`` is global after (3), so every rank skips or steps together; the bf16
+  all-gather still runs so all ranks issue the same collectives in the same order.
+
+``defer_param_gather=True`` leaves step (5) to an explicit :meth:`gather_params` call (for a
+trainer that overlaps it with the next forward pass, or a benchmark that times it separately).
+
+Gradients: ``zero_grad`` zeroes ``flat_grad`` in place and keeps the views (``set_to_none`` has
+no effect: the flat buffer is the gradient storage).  A gradient that autograd allocated
+elsewhere is copied into the flat buffer at the next statistics pass or step.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .optim import GradStats, _REGISTRY, _round_up, validate_adamw_args
+from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
+
+_ALIGN = 64
+
+
+class ShardGeometry:
+    """Flat offsets of every parameter and the owned range of one rank (pure arithmetic)."""
+
+    def __init__(self, numels: list[int], world_size: int, rank: int, align: int = _ALIGN):
+        if world_size < 1 or not 0 <= rank < world_size:
+            raise ValueError("bad world_size / rank")
+        self.numels = list(numels)
+        self.offsets = []
+        total = 0
+        for n in numels:
+            self.offsets.append(total)
+            total += _round_up(n, align)
+        self.total = total
+        self.padded = _round_up(max(total, 1), align * world_size)
+        self.shard = self.padded // world_size
+        self.world_size = world_size
+        self.rank = rank
+        self.lo = rank * self.shard
+        self.hi = self.lo + self.shard
+
+    def local_ranges(self) -> list[tuple[int, int, int]]:
+        """(slot, flat_lo, flat_hi) of every parameter clipped to the owned range; empty
+        ranges are kept (lo == hi) so every rank's table lists every slot."""
+        out = []
+        for slot, (off, n) in enumerate(zip(self.offsets, self.numels)):
+            lo, hi = max(off, self.lo), min(off + n, self.hi)
+            out.append((slot, lo, hi) if lo < hi else (slot, self.lo, self.lo))
+        return out
+
+    def owned_numel(self) -> int:
+        return sum(hi - lo for _, lo, hi in self.local_ranges())
+
+
+class CudaKernels:
+    """The product backend: the sm_100a kernels of ``lib/libb200_optim.so``."""
+
+    def make_plan(self, opt: "ZeroAdamW", ranges) -> ChunkPlan:
+        esz = opt.flat_param.element_size()
+        gd = dtype_code(opt.flat_grad.dtype)
+        pd = dtype_code(opt.flat_param.dtype)
+        entries = []
+        for slot, lo, hi in ranges:
+            n = hi - lo
+            loc = lo - opt.geom.lo
+            if n == 0:
+                entries.append(Entry(0, 0, 0, 0, 0, 0, opt._slot_group[slot], slot))
+                continue
+            master = (opt.master.data_ptr() + 4 * loc) if pd == _lib.BF16 else \
+                opt.flat_param.data_ptr() + esz * lo
+            entries.append(Entry(
+                grad=opt.flat_grad.data_ptr() + opt.flat_grad.element_size() * lo,
+                param=opt.flat_param.data_ptr() + esz * lo if pd == _lib.BF16 else 0,
+                master=master, exp_avg=opt.exp_avg.data_ptr() + 4 * loc,
+                exp_avg_sq=opt.exp_avg_sq.data_ptr() + 4 * loc, numel=n,
+                group=opt._slot_group[slot], slot=slot))
+        return ChunkPlan(opt.device, entries, len(opt.param_groups), opt.n_slots, gd, pd,
+                         opt._chunk_elems)
+
+    def grad_stats(self, plan: ChunkPlan, loss_scale, exch_local: torch.Tensor) -> None:
+        _lib.call("b2o_grad_stats", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
+                  plan.n_chunks, plan.n_slots, plan.grad_dtype,
+                  None if loss_scale is None else loss_scale.data_ptr(),
+                  plan.workspace.data_ptr(), exch_local.data_ptr(), _lib.STATS_CLEAR, None, None,
+                  stream_ptr(plan.device))
+
+    def finalize(self, exch_all: torch.Tensor, n_ranks: int, n_slots: int,
+                 out: torch.Tensor) -> None:
+        _lib.call("b2o_finalize_norm", exch_all.data_ptr(), n_ranks, n_slots, out.data_ptr(),
+                  out.data_ptr() + 4, stream_ptr(out.device))
+
+    def adamw(self, plan: ChunkPlan, groups: np.ndarray, steps: torch.Tensor, found_inf,
+              loss_scale, norm, max_norm: float) -> None:
+        _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
+                  plan.n_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
+                  plan.param_dtype, steps.data_ptr(),
+                  None if found_inf is None else found_inf.data_ptr(),
+                  None if loss_scale is None else loss_scale.data_ptr(),
+                  None if norm is None else norm.data_ptr(), float(max_norm), None,
+                  plan.workspace.data_ptr(), stream_ptr(plan.device))
+
+    def launches_per_step(self) -> int:
+        return 3  # stats, finalize, adamw
+
+
+class ZeroAdamW(torch.optim.Optimizer):
+    """ZeRO-1 sharded :class:`FusedAdamW` (same constructor arguments plus the group)."""
+
+    _b2o_fused = True
+
+    def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 1e-2, amsgrad: bool = False, *,
+                 maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
+                 differentiable: bool = False, fused: bool | None = None,
+                 process_group=None, chunk_elems: int = DEFAULT_CHUNK_ELEMS,
+                 defer_param_gather: bool = False, _kernels=None):
+        validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
+                            chunk_elems)
+        defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
+                        weight_decay=weight_decay, amsgrad=False, maximize=False,
+                        foreach=foreach, capturable=capturable, differentiable=False,
+                        fused=fused, decoupled_weight_decay=True)
+        super().__init__(params, defaults)
+        self._step_supports_amp_scaling = True
+        self._chunk_elems = int(chunk_elems)
+        self.defer_param_gather = defer_param_gather
+        if process_group is None and dist.is_available() and dist.is_initialized():
+            process_group = dist.group.WORLD
+        self.pg = process_group
+        self.world_size = dist.get_world_size(process_group) if process_group is not None else 1
+        self.rank = dist.get_rank(process_group) if process_group is not None else 0
+        plist = [p for g in self.param_groups for p in g["params"]]
+        if not plist:
+            raise ValueError("ZeroAdamW got no parameters")
+        devs = {p.device for p in plist}
+        dts = {p.dtype for p in plist}
+        if len(devs) != 1 or len(dts) != 1:
+            raise RuntimeError("ZeroAdamW needs every parameter on one device with one dtype")
+        self.device = next(iter(devs))
+        dtype = next(iter(dts))
+        dtype_code(dtype)
+        self._kernels = _kernels if _kernels is not None else CudaKernels()
+        if _kernels is None and self.device.type != "cuda":
+            raise RuntimeError("ZeroAdamW runs on CUDA devices only; there is no CPU path")
+        self.params = plist
+        self.n_slots = len(plist)
+        self._slot_group = [gi for gi, g in enumerate(self.param_groups) for _ in g["params"]]
+        self.geom = ShardGeometry([p.numel() for p in plist], self.world_size, self.rank)
+        S = self.geom.shard
+        with torch.no_grad():
+            self.flat_param = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
+            self.flat_grad = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
+            self._grad_views = []
+            for p, off in zip(plist, self.geom.offsets):
+                view = self.flat_param[off:off + p.numel()].view(p.shape)
+                view.copy_(p.detach())
+                p.data = view
+                self._grad_views.append(self.flat_grad[off:off + p.numel()].view(p.shape))
+            own = self.flat_param[self.geom.lo:self.geom.hi]
+            if dtype == torch.bfloat16:
+                self.master = own.float()
+            else:
+                self.master = own  # fp32 parameters are their own masters
+            self.exp_avg = torch.zeros(S, dtype=torch.float32, device=self.device)
+            self.exp_avg_sq = torch.zeros(S, dtype=torch.float32, device=self.device)
+            self.steps = torch.zeros(self.n_slots, dtype=torch.float32, device=self.device)
+            self.exch_local = torch.zeros(self.n_slots + 1, dtype=torch.float64,
+                                          device=self.device)
+            self.exch_all = torch.zeros(self.world_size * (self.n_slots + 1), dtype=torch.float64,
+                                        device=self.device)
+        for p, v in zip(plist, self._grad_views):
+            p.grad = v
+        self._plan = self._kernels.make_plan(self, self.geom.local_ranges())
+        self._plans = [self._plan]
+        self._pending: GradStats | None = None
+        self.last_allgather_report = None
+        _REGISTRY.add(self)
+
+    # ------------------------------------------------------------------------------------
+    # helpers used by the benchmark and by trainers
+    # ------------------------------------------------------------------------------------
+
+    def managed_params(self) -> list[torch.Tensor]:
+        return list(self.params)
+
+    def make_flat_grads_(self) -> list[torch.Tensor]:
+        for p, v in zip(self.params, self._grad_views):
+            p.grad = v
+        return list(self._grad_views)
+
+    def local_numel(self) -> int:
+        return self.geom.owned_numel()
+
+    def owned_param_shard(self) -> torch.Tensor:
+        return self.flat_param[self.geom.lo:self.geom.hi]
+
+    def gather_params(self) -> None:
+        """Refresh every rank's ``flat_param`` with the other ranks' updated shards."""
+        if self.world_size > 1:
+            dist.all_gather_into_tensor(self.flat_param, self.owned_param_shard(), group=self.pg)
+
+    # ------------------------------------------------------------------------------------
+    # torch.optim.Optimizer surface
+    # ------------------------------------------------------------------------------------
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        with torch.no_grad():
+            self.flat_grad.zero_()
+        for p, v in zip(self.params, self._grad_views):
+            p.grad = v
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        self._adopt_grads()
+        pend = self._pending
+        self._pending = None
+        found_inf = getattr(self, "found_inf", None)
+        if found_inf is not None:
+            found_inf = found_inf.to(device=self.device, dtype=torch.float32)
+        loss_scale = pend.loss_scale if pend is not None else None
+        grad_scale = getattr(self, "grad_scale", None)
+        if loss_scale is None and grad_scale is not None:
+            loss_scale = grad_scale.to(device=self.device, dtype=torch.float32)
+        norm = pend.norm if (pend is not None and pend.max_norm is not None) else None
+        max_norm = pend.max_norm if norm is not None else 0.0
+        self._kernels.adamw(self._plan, self._group_array(), self.steps, found_inf, loss_scale,
+                            norm, max_norm)
+        if not self.defer_param_gather:
+            self.gather_params()
+        return loss
+
+    def state_dict(self) -> dict[str, Any]:
+        """This rank's shard: the reference's param_groups plus the owned fp32 state."""
+        groups = []
+        idx = 0
+        for g in self.param_groups:
+            packed = {k: v for k, v in g.items() if k != "params"}
+            packed["params"] = list(range(idx, idx + len(g["params"])))
+            idx += len(g["params"])
+            groups.append(packed)
+        return {"state": {}, "param_groups": groups,
+                "zero1": {"world_size": self.world_size, "rank": self.rank,
+                          "shard": [self.geom.lo, self.geom.hi],
+                          "numels": self.geom.numels,
+                          "master": self.master.detach().clone(),
+                          "exp_avg": self.exp_avg.detach().clone(),
+                          "exp_avg_sq": self.exp_avg_sq.detach().clone(),
+                          "steps": self.steps.detach().clone()}}
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        z = state_dict.get("zero1")
+        if z is None:
+            raise ValueError("not a ZeroAdamW shard state_dict")
+        if z["world_size"] != self.world_size or list(z["shard"]) != [self.geom.lo, self.geom.hi] \
+                or list(z["numels"]) != self.geom.numels:
+            raise ValueError("shard layout differs (world size or parameter list changed)")
+        for g, s in zip(self.param_groups, state_dict["param_groups"]):
+            for k, v in s.items():
+                if k != "params":
+                    g[k] = v
+        with torch.no_grad():
+            self.master.copy_(z["master"])
+            self.exp_avg.copy_(z["exp_avg"])
+            self.exp_avg_sq.copy_(z["exp_avg_sq"])
+            self.steps.copy_(z["steps"])
+            if self.flat_param.dtype == torch.bfloat16:
+                self.owned_param_shard().copy_(self.master)
+        self.gather_params()
+
+    # ------------------------------------------------------------------------------------
+    # GradScaler / clip_grad_norm_ hooks
+    # ------------------------------------------------------------------------------------
+
+    @torch.no_grad()
+    def _grad_stats(self, loss_scale: torch.Tensor | None) -> GradStats:
+        self._adopt_grads()
+        if loss_scale is not None:
+            loss_scale = loss_scale.to(device=self.device, dtype=torch.float32)
+        out = torch.zeros(2, dtype=torch.float32, device=self.device)
+        self._kernels.grad_stats(self._plan, loss_scale, self.exch_local)
+        if self.world_size > 1:
+            dist.all_gather_into_tensor(self.exch_all, self.exch_local, group=self.pg)
+            exch = self.exch_all
+        else:
+            exch = self.exch_local
+        self._kernels.finalize(exch, self.world_size, self.n_slots, out)
+        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale)
+        return self._pending
+
+    def _owns_exactly(self, params) -> bool:
+        mine = {id(p) for p in self.params}
+        theirs = {id(p) for p in params if p.grad is not None}
+        return mine == theirs
+
+    def _adopt_grads(self) -> None:
+        for i, (p, v) in enumerate(zip(self.params, self._grad_views)):
+            g = p.grad
+            if g is v:
+                continue
+            if g is None:
+                raise RuntimeError("ZeroAdamW needs a gradient for every parameter")
+            with torch.no_grad():
+                v.copy_(g)
+            p.grad = v
+
+    def _group_array(self) -> np.ndarray:
+        arr = np.zeros(len(self.param_groups), dtype=_lib.GROUP_DTYPE)
+        if len(arr) > _lib.MAX_GROUPS:
+            raise ValueError(f"at most {_lib.MAX_GROUPS} param groups are supported")
+        for i, g in enumerate(self.param_groups):
+            b1, b2 = g["betas"]
+            arr[i] = (float(g["lr"]), float(b1), float(b2), float(g["eps"]),
+                      float(g["weight_decay"]))
+        return arr

@@ -1,0 +1,122 @@
+"""ZeroAdamW on GPUs: one rank must reproduce FusedAdamW bit for bit; two NCCL ranks (when two
+GPUs are visible) must reproduce the one-GPU result."""
+
+from __future__ import annotations
+
+import datetime
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(300, 129), (129,), (5,), (1024, 64), (3, 3, 3), (70001,), (0,), (4096, 33)]
+
+
+def _init(device, dtype=torch.bfloat16):
+    gen = torch.Generator().manual_seed(77)
+    w0 = [torch.randn(s, generator=gen) * 0.02 for s in SHAPES]
+    params = [torch.nn.Parameter(w.to(dtype).to(device)) for w in w0]
+    groups = [{"params": [p for p, s in zip(params, SHAPES) if len(s) >= 2], "weight_decay": 0.1},
+              {"params": [p for p, s in zip(params, SHAPES) if len(s) < 2], "weight_decay": 0.0,
+               "lr": 1e-3}]
+    return w0, params, groups
+
+
+def _grads(step, dtype, device):
+    gen = torch.Generator().manual_seed(500 + step)
+    gs = [(torch.randn(s, generator=gen) * 0.05 * 2.0 ** 14).to(dtype) for s in SHAPES]
+    if step == 3:
+        gs[5][60000] = float("nan")
+    return [g.to(device) for g in gs]
+
+
+def _run(opt, params, scaler, device, dtype, steps=6, copy_grads=False):
+    from minigpt_train_infra_b200 import clip_grad_norm_
+    norms = []
+    for s in range(steps):
+        for p, g in zip(params, _grads(s, dtype, device)):
+            if copy_grads:
+                p.grad.copy_(g)
+            else:
+                p.grad = g
+        scaler.unscale_(opt)
+        norms.append(clip_grad_norm_(params, 1.0))
+        scaler.step(opt)
+        scaler.update()
+    return [float(n) for n in norms]
+
+
+def test_zero_world1_matches_fused_bit_for_bit():
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, ZeroAdamW
+    device = torch.device("cuda", 0)
+    results = []
+    for cls in (FusedAdamW, ZeroAdamW):
+        _, params, groups = _init(device)
+        opt = cls(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+        sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+        sc.scale(torch.ones((), device=device))
+        norms = _run(opt, params, sc, device, torch.bfloat16)
+        torch.cuda.synchronize()
+        results.append((norms, [p.detach().clone() for p in params], float(sc.get_scale())))
+    (n0, p0, s0), (n1, p1, s1) = results
+    assert s0 == s1
+    np.testing.assert_array_equal(np.array(n0), np.array(n1))
+    for a, b in zip(p0, p1):
+        assert torch.equal(a, b)
+
+
+def _nccl_worker(rank, world, port, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [here, os.path.dirname(here)]
+    import torch.distributed as dist
+    from minigpt_train_infra_b200 import GradScaler, ZeroAdamW
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=device)
+    try:
+        _, params, groups = _init(device)
+        opt = ZeroAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+        sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+        sc.scale(torch.ones((), device=device))
+        norms = _run(opt, params, sc, device, torch.bfloat16, copy_grads=True)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"nccl{rank}.npz"), norms=np.array(norms),
+                 scale=float(sc.get_scale()),
+                 flat=opt.flat_param.float().cpu().numpy(), steps=opt.steps.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_zero_two_nccl_ranks_match_one_gpu(tmp_path):
+    from minigpt_train_infra_b200 import GradScaler, ZeroAdamW
+    port = 29500 + os.getpid() % 1000
+    mp.start_processes(_nccl_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    device = torch.device("cuda", 0)
+    _, params, groups = _init(device)
+    opt = ZeroAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+    sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+    sc.scale(torch.ones((), device=device))
+    norms = _run(opt, params, sc, device, torch.bfloat16, copy_grads=True)
+    flat1 = opt.flat_param.float().cpu().numpy()
+    for r in range(2):
+        z = np.load(tmp_path / f"nccl{r}.npz")
+        assert float(z["scale"]) == float(sc.get_scale())
+        np.testing.assert_array_equal(z["steps"], opt.steps.cpu().numpy())
+        for a, b in zip(z["norms"], norms):
+            assert (np.isnan(a) and np.isnan(b)) or abs(a - b) <= 2 * np.spacing(np.float32(b))
+        n = min(len(flat1), len(z["flat"]))
+        # same values everywhere both layouts hold parameters (padding differs with the world)
+        for p, off in zip(opt.params, opt.geom.offsets):
+            np.testing.assert_array_equal(z["flat"][off:off + p.numel()],
+                                          flat1[off:off + p.numel()])
