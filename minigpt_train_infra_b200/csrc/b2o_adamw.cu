@@ -35,13 +35,18 @@ struct ChunkScalars {
   int small_w1;
 };
 
-__device__ __forceinline__ void chunk_scalars(const b2o_group& hp, float step_old,
-                                              ChunkScalars& s) {
-  // Python evaluates these in double, one rounding per operator; the explicit _rn forms keep
-  // nvcc from contracting `1 - lr*wd` into an fma.
+// The per-tensor scalars of one step, formed by a whole warp: lane 0 evaluates beta1^step and
+// lane 1 beta2^step (one pow per lane, no divergence) and the results are shuffled to every lane.
+// Python evaluates these in double with one rounding per operator; the explicit _rn forms keep
+// nvcc from contracting `1 - lr*wd` into an fma.
+__device__ __forceinline__ void warp_scalars(const b2o_group& hp, float step_old, int lane,
+                                             ChunkScalars& s) {
   const double step = (double)__fadd_rn(step_old, 1.0f);  // torch: step_t += 1 (fp32), .item()
-  const double bc1 = __dsub_rn(1.0, pow(hp.beta1, step));
-  const double bc2 = __dsub_rn(1.0, pow(hp.beta2, step));
+  const double pw = pow(lane == 0 ? hp.beta1 : hp.beta2, step);
+  const double p1 = __shfl_sync(0xffffffffu, pw, 0);
+  const double p2 = __shfl_sync(0xffffffffu, pw, 1);
+  const double bc1 = __dsub_rn(1.0, p1);
+  const double bc2 = __dsub_rn(1.0, p2);
   s.decay = (float)__dsub_rn(1.0, __dmul_rn(hp.lr, hp.weight_decay));
   s.w1 = (float)__dsub_rn(1.0, hp.beta1);
   s.w1m1 = __fsub_rn(s.w1, 1.0f);
@@ -71,90 +76,138 @@ __device__ __forceinline__ float clip_coefficient(float norm, float max_norm) {
   return c > 1.0f ? 1.0f : c;
 }
 
-template <class G, bool BF16_PARAM, int U>
-__global__ void __launch_bounds__(kThreads)
+// Quads (4 consecutive elements) each thread keeps in flight per loop iteration, and the CTAs per
+// SM the register budget is sized for.  Both are build-time knobs; the defaults were measured.
+#ifndef B2O_ADAMW_QUADS
+#define B2O_ADAMW_QUADS 2
+#endif
+#ifndef B2O_ADAMW_MIN_CTAS
+#define B2O_ADAMW_MIN_CTAS 4
+#endif
+// Chunk scheduling of the update pass: 0 static round-robin over CTAs, 1 dynamic per CTA,
+// 2 dynamic per warp (both dynamic modes take chunks in order from a counter in the workspace,
+// so the chunks in flight stay a compact window of each array).
+#ifndef B2O_ADAMW_SCHED
+#define B2O_ADAMW_SCHED 1
+#endif
+
+template <class G, bool BF16_PARAM, int Q>
+__global__ void __launch_bounds__(kThreads, B2O_ADAMW_MIN_CTAS)
 adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
              const b2o_chunk* __restrict__ chunks, int64_t n_chunks, GroupArgs groups,
              float* __restrict__ steps, const float* __restrict__ found_inf,
              const float* __restrict__ loss_scale, const float* __restrict__ norm_p,
              float max_norm, float* clip_coef_out, Workspace ws) {
   if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step: no traffic at all
-  __shared__ ChunkScalars sc;
   __shared__ int is_last;
   const float inv = inv_scale_of(loss_scale);
   const float coef = norm_p ? clip_coefficient(*norm_p, max_norm) : 1.0f;
   if (clip_coef_out && blockIdx.x == 0 && threadIdx.x == 0) *clip_coef_out = coef;
+  const int lane = threadIdx.x & 31;
 
+  // Per-tensor state, refreshed only when the chunk sequence enters another tensor.  Every
+  // thread of a scheduling unit (the CTA, or the warp when B2O_ADAMW_SCHED == 2) walks the same
+  // chunks, so the refresh branch is uniform within it.
+  int cur = -1;
+  ChunkScalars s{};
+  const void* gp = nullptr;
+  float* wp = nullptr;
+  float* mp = nullptr;
+  float* vp = nullptr;
+  uint16_t* pp = nullptr;
+  int flags = 0;
+#if B2O_ADAMW_SCHED == 0
+  // static: CTA b takes chunks b, b + grid, b + 2*grid, ...
+  constexpr int kUnit = kThreads;
+  const int utid = threadIdx.x;
+  b2o_chunk next{};
+  if (blockIdx.x < n_chunks) next = chunks[blockIdx.x];
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const b2o_chunk ch = next;
+    if (c + gridDim.x < n_chunks) next = chunks[c + gridDim.x];  // prefetch the next record
+#elif B2O_ADAMW_SCHED == 1
+  // dynamic per CTA: thread 0 takes the next chunk from a global counter one chunk ahead
+  constexpr int kUnit = kThreads;
+  const int utid = threadIdx.x;
+  __shared__ unsigned int s_tile[2];
+  if (threadIdx.x == 0) s_tile[0] = atomicAdd(ws.adamw_tile, 1u);
+  __syncthreads();
+  int buf = 0;
+  for (int64_t c = s_tile[0]; c < n_chunks; ) {
+    if (threadIdx.x == 0) s_tile[buf ^ 1] = atomicAdd(ws.adamw_tile, 1u);
     const b2o_chunk ch = chunks[c];
-    const b2o_tensor& t = tensors[ch.tensor];
-    __syncthreads();  // previous chunk's readers of `sc` are done
-    if (threadIdx.x == 0) chunk_scalars(groups.g[t.group], steps[t.slot], sc);
-    __syncthreads();
-    const ChunkScalars s = sc;
-    const void* gp = t.grad;
-    float* wp = t.master;
-    float* mp = t.exp_avg;
-    float* vp = t.exp_avg_sq;
-    uint16_t* pp = static_cast<uint16_t*>(t.param);
+#else
+  // dynamic per warp: lane 0 takes the next chunk one chunk ahead, shuffled to the warp
+  constexpr int kUnit = 32;
+  const int utid = lane;
+  unsigned int tile = 0;
+  if (lane == 0) tile = atomicAdd(ws.adamw_tile, 1u);
+  tile = __shfl_sync(0xffffffffu, tile, 0);
+  for (int64_t c = tile; c < n_chunks; ) {
+    unsigned int nt = 0;
+    if (lane == 0) nt = atomicAdd(ws.adamw_tile, 1u);
+    const b2o_chunk ch = chunks[c];
+#endif
+    if (ch.tensor != cur) {
+      cur = ch.tensor;
+      const b2o_tensor& t = tensors[cur];
+      gp = t.grad;
+      wp = t.master;
+      mp = t.exp_avg;
+      vp = t.exp_avg_sq;
+      pp = static_cast<uint16_t*>(t.param);
+      flags = t.flags;
+      warp_scalars(groups.g[t.group], steps[t.slot], lane, s);
+    }
     const int64_t n = ch.end - ch.begin;
     int64_t done = 0;
-    if (t.flags & B2O_FLAG_VECTOR) {
-      const int64_t nv = n & ~int64_t(B2O_VEC - 1);
-      done = nv;
-      constexpr int64_t kStride = int64_t(kThreads) * B2O_VEC;
-      for (int64_t i0 = int64_t(threadIdx.x) * B2O_VEC; i0 < nv; i0 += kStride * U) {
-        typename G::vec_t gv[U];
-        float4 w[U][2], m[U][2], v[U][2];
-        // Issue every load of the U vectors before any arithmetic.
+    if (flags & B2O_FLAG_VECTOR) {
+      const int64_t nq = n >> 2;
+      done = nq << 2;
+      for (int64_t q0 = utid; q0 < nq; q0 += int64_t(kUnit) * Q) {
+        typename G::quad_t gq[Q];
+        float4 w[Q], m[Q], v[Q];
+        // Issue every load of the Q quads before any arithmetic.
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t i = i0 + u * kStride;
-          if (i < nv) {
-            const int64_t e = ch.begin + i;
-            gv[u] = G::load(gp, e);
-            const float4* w4 = reinterpret_cast<const float4*>(wp + e);
-            const float4* m4 = reinterpret_cast<const float4*>(mp + e);
-            const float4* v4 = reinterpret_cast<const float4*>(vp + e);
-            w[u][0] = ld_stream(w4); w[u][1] = ld_stream(w4 + 1);
-            m[u][0] = ld_stream(m4); m[u][1] = ld_stream(m4 + 1);
-            v[u][0] = ld_stream(v4); v[u][1] = ld_stream(v4 + 1);
+        for (int u = 0; u < Q; ++u) {
+          const int64_t q = q0 + int64_t(u) * kUnit;
+          if (q < nq) {
+            const int64_t e = ch.begin + 4 * q;
+            gq[u] = G::load4(gp, e);
+            w[u] = ld_stream(reinterpret_cast<const float4*>(wp + e));
+            m[u] = ld_stream(reinterpret_cast<const float4*>(mp + e));
+            v[u] = ld_stream(reinterpret_cast<const float4*>(vp + e));
           }
         }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t i = i0 + u * kStride;
-          if (i < nv) {
-            const int64_t e = ch.begin + i;
-            float x[B2O_VEC];
-            G::unpack(gv[u], x);
-            float* wf = reinterpret_cast<float*>(w[u]);
-            float* mf = reinterpret_cast<float*>(m[u]);
-            float* vf = reinterpret_cast<float*>(v[u]);
+        for (int u = 0; u < Q; ++u) {
+          const int64_t q = q0 + int64_t(u) * kUnit;
+          if (q < nq) {
+            const int64_t e = ch.begin + 4 * q;
+            float x[4];
+            G::unpack4(gq[u], x);
+            float* wf = reinterpret_cast<float*>(&w[u]);
+            float* mf = reinterpret_cast<float*>(&m[u]);
+            float* vf = reinterpret_cast<float*>(&v[u]);
 #pragma unroll
-            for (int k = 0; k < B2O_VEC; ++k) {
+            for (int k = 0; k < 4; ++k) {
               const float g = __fmul_rn(__fmul_rn(x[k], inv), coef);
               adamw_elem(s, g, wf[k], mf[k], vf[k]);
             }
-            float4* w4 = reinterpret_cast<float4*>(wp + e);
-            float4* m4 = reinterpret_cast<float4*>(mp + e);
-            float4* v4 = reinterpret_cast<float4*>(vp + e);
-            st_stream(w4, w[u][0]); st_stream(w4 + 1, w[u][1]);
-            st_stream(m4, m[u][0]); st_stream(m4 + 1, m[u][1]);
-            st_stream(v4, v[u][0]); st_stream(v4 + 1, v[u][1]);
+            st_stream(reinterpret_cast<float4*>(wp + e), w[u]);
+            st_stream(reinterpret_cast<float4*>(mp + e), m[u]);
+            st_stream(reinterpret_cast<float4*>(vp + e), v[u]);
             if (BF16_PARAM) {
-              uint4 q;
-              q.x = pack_bf16x2(wf[0], wf[1]);
-              q.y = pack_bf16x2(wf[2], wf[3]);
-              q.z = pack_bf16x2(wf[4], wf[5]);
-              q.w = pack_bf16x2(wf[6], wf[7]);
-              st_stream(reinterpret_cast<uint4*>(pp + e), q);
+              uint2 pq;
+              pq.x = pack_bf16x2(wf[0], wf[1]);
+              pq.y = pack_bf16x2(wf[2], wf[3]);
+              __stcs(reinterpret_cast<uint2*>(pp + e), pq);
             }
           }
         }
       }
     }
-    for (int64_t i = done + threadIdx.x; i < n; i += kThreads) {
+    for (int64_t i = done + utid; i < n; i += kUnit) {
       const int64_t e = ch.begin + i;
       bool unused = false;
       const float g = __fmul_rn(__fmul_rn(G::load1(gp, e, unused), inv), coef);
@@ -165,6 +218,13 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
       vp[e] = v;
       if (BF16_PARAM) pp[e] = to_bf16_bits(w);
     }
+#if B2O_ADAMW_SCHED == 1
+    __syncthreads();  // s_tile[buf ^ 1] is written; every thread moves on together
+    buf ^= 1;
+    c = s_tile[buf];
+#elif B2O_ADAMW_SCHED == 2
+    c = __shfl_sync(0xffffffffu, nt, 0);
+#endif
   }
 
   // Completion ticket; the last CTA advances the step counters after every CTA has read them.
@@ -178,7 +238,10 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
     const int slot = tensors[ti].slot;
     steps[slot] = __fadd_rn(__ldcg(steps + slot), 1.0f);
   }
-  if (threadIdx.x == 0) *ws.adamw_done = 0u;
+  if (threadIdx.x == 0) {
+    *ws.adamw_tile = 0u;
+    *ws.adamw_done = 0u;
+  }
 }
 
 template <class G, bool P>
@@ -186,9 +249,10 @@ int launch_adamw(cudaStream_t s, const b2o_tensor* tensors, int n_tensors,
                  const b2o_chunk* chunks, int64_t n_chunks, const GroupArgs& ga, float* steps,
                  const float* found_inf, const float* loss_scale, const float* norm, float max_norm,
                  float* coef_out, Workspace ws) {
-  const int grid = stream_grid((const void*)adamw_kernel<G, P, 2>, kThreads, n_chunks);
+  constexpr int Q = B2O_ADAMW_QUADS;
+  const int grid = stream_grid((const void*)adamw_kernel<G, P, Q>, kThreads, n_chunks);
   if (grid <= 0) return B2O_ERR_CUDA;
-  adamw_kernel<G, P, 2><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks, ga, steps,
+  adamw_kernel<G, P, Q><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks, ga, steps,
                                                   found_inf, loss_scale, norm, max_norm, coef_out, ws);
   return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
 }

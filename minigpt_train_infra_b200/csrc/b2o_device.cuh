@@ -75,6 +75,14 @@ struct GradBF16 {
     bad |= (b & 0x7f80u) == 0x7f80u;
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
   }
+  // Four consecutive elements (8 bytes); a warp's 32 quads cover 256 contiguous bytes.
+  using quad_t = uint2;
+  static __device__ __forceinline__ quad_t load4(const void* base, int64_t i) {
+    return __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + i));
+  }
+  static __device__ __forceinline__ void unpack4(const quad_t& q, float (&x)[4]) {
+    x[0] = bf16_lo(q.x); x[1] = bf16_hi(q.x); x[2] = bf16_lo(q.y); x[3] = bf16_hi(q.y);
+  }
 };
 
 struct GradF32 {
@@ -96,6 +104,13 @@ struct GradF32 {
     float f = static_cast<const float*>(base)[i];
     bad |= (__float_as_uint(f) & 0x7f800000u) == 0x7f800000u;
     return f;
+  }
+  using quad_t = float4;
+  static __device__ __forceinline__ quad_t load4(const void* base, int64_t i) {
+    return __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(base) + i));
+  }
+  static __device__ __forceinline__ void unpack4(const quad_t& q, float (&x)[4]) {
+    x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
   }
 };
 
@@ -137,6 +152,7 @@ struct Workspace {
   unsigned int* stats_done;
   unsigned int* stats_nonfinite;
   unsigned int* adamw_done;
+  unsigned int* adamw_tile;  // next chunk to hand out when the update pass schedules dynamically
   double* chunk_sums;
   double* exch;
 };
@@ -149,6 +165,7 @@ __host__ __device__ inline Workspace carve_workspace(void* ws, int64_t n_chunks)
   w.stats_done = c + 0;
   w.stats_nonfinite = c + 1;
   w.adamw_done = c + 2;
+  w.adamw_tile = c + 3;
   w.chunk_sums = reinterpret_cast<double*>(static_cast<char*>(ws) + ws_counter_bytes());
   w.exch = w.chunk_sums + n_chunks;
   return w;

@@ -43,7 +43,13 @@ __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slo
   }
 }
 
-template <class G>
+// Vectors (8 elements, 16 bytes of bf16) each thread keeps in flight per loop iteration; a
+// build-time knob, the default was measured.
+#ifndef B2O_STATS_UNROLL
+#define B2O_STATS_UNROLL 8
+#endif
+
+template <class G, int U = B2O_STATS_UNROLL>
 __global__ void __launch_bounds__(kThreads)
 grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
                   const b2o_chunk* __restrict__ chunks, int64_t n_chunks, int n_slots,
@@ -64,18 +70,31 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
     if (t.flags & B2O_FLAG_VECTOR) {
       const int64_t nv = n & ~int64_t(B2O_VEC - 1);
       done = nv;
-      for (int64_t i = int64_t(threadIdx.x) * B2O_VEC; i < nv; i += int64_t(kThreads) * B2O_VEC) {
-        const typename G::vec_t v = G::load(g, ch.begin + i);
-        bad |= G::nonfinite(v);
-        float x[B2O_VEC];
-        G::unpack(v, x);
-        float s = 0.0f;
+      constexpr int64_t kStride = int64_t(kThreads) * B2O_VEC;
+      for (int64_t i0 = int64_t(threadIdx.x) * B2O_VEC; i0 < nv; i0 += kStride * U) {
+        typename G::vec_t v[U];
+        // Issue all U loads before reducing any of them.
 #pragma unroll
-        for (int k = 0; k < B2O_VEC; ++k) {
-          const float u = __fmul_rn(x[k], inv);
-          s = __fmaf_rn(u, u, s);
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * kStride;
+          if (i < nv) v[u] = G::load(g, ch.begin + i);
         }
-        acc += (double)s;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * kStride;
+          if (i < nv) {
+            bad |= G::nonfinite(v[u]);
+            float x[B2O_VEC];
+            G::unpack(v[u], x);
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < B2O_VEC; ++k) {
+              const float e = __fmul_rn(x[k], inv);
+              s = __fmaf_rn(e, e, s);
+            }
+            acc += (double)s;
+          }
+        }
       }
     }
     for (int64_t i = done + threadIdx.x; i < n; i += kThreads) {

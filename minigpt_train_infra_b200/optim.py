@@ -75,7 +75,7 @@ def validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differe
     if amsgrad or maximize or differentiable:
         raise NotImplementedError("the fused optimizers support amsgrad=False, maximize=False, "
                                   "differentiable=False only")
-    if chunk_elems <= 0 or chunk_elems % _lib.VEC:
+    if chunk_elems is not None and (chunk_elems <= 0 or chunk_elems % _lib.VEC):
         raise ValueError("chunk_elems must be a positive multiple of 8")
 
 
@@ -88,7 +88,7 @@ class FusedAdamW(torch.optim.Optimizer):
                  eps: float = 1e-8, weight_decay: float = 1e-2, amsgrad: bool = False, *,
                  maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
                  differentiable: bool = False, fused: bool | None = None,
-                 chunk_elems: int = DEFAULT_CHUNK_ELEMS):
+                 chunk_elems: int | None = DEFAULT_CHUNK_ELEMS):
         validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
                             chunk_elems)
         defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
@@ -97,7 +97,7 @@ class FusedAdamW(torch.optim.Optimizer):
                         fused=fused, decoupled_weight_decay=True)
         super().__init__(params, defaults)
         self._step_supports_amp_scaling = True
-        self._chunk_elems = int(chunk_elems)
+        self._chunk_elems = None if chunk_elems is None else int(chunk_elems)
         self._store: _FlatStore | None = None
         self._plans: list[ChunkPlan] | None = None
         self._plan_key: tuple | None = None
@@ -150,8 +150,8 @@ class FusedAdamW(torch.optim.Optimizer):
         groups = self._group_array()
         stream = stream_ptr(device)
         for plan in plans:
-            _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
-                      plan.n_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
+            _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors,
+                      plan.update_chunks_ptr, plan.n_update_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
                       plan.param_dtype, store.steps.data_ptr(),
                       None if found_inf is None else found_inf.data_ptr(),
                       None if loss_scale is None else loss_scale.data_ptr(),

@@ -114,8 +114,8 @@ class CudaKernels:
 
     def adamw(self, plan: ChunkPlan, groups: np.ndarray, steps: torch.Tensor, found_inf,
               loss_scale, norm, max_norm: float) -> None:
-        _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr,
-                  plan.n_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
+        _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors, plan.update_chunks_ptr,
+                  plan.n_update_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
                   plan.param_dtype, steps.data_ptr(),
                   None if found_inf is None else found_inf.data_ptr(),
                   None if loss_scale is None else loss_scale.data_ptr(),
@@ -135,7 +135,7 @@ class ZeroAdamW(torch.optim.Optimizer):
                  eps: float = 1e-8, weight_decay: float = 1e-2, amsgrad: bool = False, *,
                  maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
                  differentiable: bool = False, fused: bool | None = None,
-                 process_group=None, chunk_elems: int = DEFAULT_CHUNK_ELEMS,
+                 process_group=None, chunk_elems: int | None = DEFAULT_CHUNK_ELEMS,
                  defer_param_gather: bool = False, _kernels=None):
         validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
                             chunk_elems)
@@ -145,7 +145,7 @@ class ZeroAdamW(torch.optim.Optimizer):
                         fused=fused, decoupled_weight_decay=True)
         super().__init__(params, defaults)
         self._step_supports_amp_scaling = True
-        self._chunk_elems = int(chunk_elems)
+        self._chunk_elems = None if chunk_elems is None else int(chunk_elems)
         self.defer_param_gather = defer_param_gather
         if process_group is None and dist.is_available() and dist.is_initialized():
             process_group = dist.group.WORLD
