@@ -153,6 +153,7 @@ struct Workspace {
   unsigned int* stats_nonfinite;
   unsigned int* adamw_done;
   unsigned int* adamw_tile;  // next chunk to hand out when the update pass schedules dynamically
+  unsigned int* stats_tile;  // the same for the statistics pass
   double* chunk_sums;
   double* exch;
 };
@@ -166,6 +167,7 @@ __host__ __device__ inline Workspace carve_workspace(void* ws, int64_t n_chunks)
   w.stats_nonfinite = c + 1;
   w.adamw_done = c + 2;
   w.adamw_tile = c + 3;
+  w.stats_tile = c + 4;
   w.chunk_sums = reinterpret_cast<double*>(static_cast<char*>(ws) + ws_counter_bytes());
   w.exch = w.chunk_sums + n_chunks;
   return w;

@@ -46,7 +46,11 @@ __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slo
 // Vectors (8 elements, 16 bytes of bf16) each thread keeps in flight per loop iteration; a
 // build-time knob, the default was measured.
 #ifndef B2O_STATS_UNROLL
-#define B2O_STATS_UNROLL 8
+#define B2O_STATS_UNROLL 4
+#endif
+// Chunk scheduling: 0 static round-robin over CTAs, 1 dynamic in-order from a counter.
+#ifndef B2O_STATS_SCHED
+#define B2O_STATS_SCHED 1
 #endif
 
 template <class G, int U = B2O_STATS_UNROLL>
@@ -60,7 +64,18 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
   const float inv = inv_scale_of(loss_scale);
   bool bad = false;
 
+#if B2O_STATS_SCHED == 1
+  // dynamic: thread 0 takes the next chunk from a global counter one chunk ahead, so the
+  // chunks being read stay a compact window of the gradient buffer
+  __shared__ unsigned int s_tile[2];
+  if (threadIdx.x == 0) s_tile[0] = atomicAdd(ws.stats_tile, 1u);
+  __syncthreads();
+  int buf = 0;
+  for (int64_t c = s_tile[0]; c < n_chunks;) {
+    if (threadIdx.x == 0) s_tile[buf ^ 1] = atomicAdd(ws.stats_tile, 1u);
+#else
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+#endif
     const b2o_chunk ch = chunks[c];
     const b2o_tensor& t = tensors[ch.tensor];
     const void* g = t.grad;
@@ -103,6 +118,11 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
     }
     const double total = block_sum(acc, scratch);
     if (threadIdx.x == 0) ws.chunk_sums[c] = total;
+#if B2O_STATS_SCHED == 1
+    __syncthreads();  // s_tile[buf ^ 1] is written; every thread moves on together
+    buf ^= 1;
+    c = s_tile[buf];
+#endif
   }
 
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(ws.stats_nonfinite, 1u);
@@ -129,6 +149,7 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
   if (threadIdx.x == 0) {
     const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
     if (nf) exch[n_slots] += 1.0;
+    *ws.stats_tile = 0u;
     *ws.stats_done = 0u;
   }
   __threadfence();
