@@ -37,6 +37,11 @@ METRIC = "fused AdamW step Gparams/s and HBM GB/s vs peak at 1/2/4/8 B200"
 ADAMW_BYTES = 28   # read g(2)+w,m,v(12); write w,m,v(12)+bf16 param(2)
 STATS_BYTES = 2    # read g
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes per parameter of one adamw_kernel launch, from ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum = 940.43 MB + 882.66 MB over 2**26 params; profiles/
+# adamw_kernel_flat_2_26_full.md).  The full workload is too large to capture under the profiler's
+# size rule, so the per-parameter figure of the small capture is scaled by the params per launch.
+NCU_TRAFFIC_BYTES_PER_PARAM = (940.429824e6 + 882.656768e6) / 2 ** 26
 LR, BETAS, EPS, WD, CLIP = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
 SCALES = {"qwen3_8b": 2.0 ** 15}
 GRAD_STD = {"flat_2_28": 1e-2, "flat_2_26": 1e-2}
@@ -380,7 +385,9 @@ def run_ours(args) -> None:
                          "peak": peak, "peak_kind": f"{peak_kind} copy bandwidth",
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "bytes_per_param": ADAMW_BYTES, "params_per_launch": P_local,
-                         "traffic": None},
+                         "traffic": round(NCU_TRAFFIC_BYTES_PER_PARAM * P_local),
+                         "traffic_source": "ncu dram read+write bytes per param of the 2**26 "
+                                           "capture x params per launch"},
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
             "e2e": e2e,
