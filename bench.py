@@ -395,7 +395,7 @@ def run_ours(args) -> None:
         }
         if ws > 1:
             line["allgather"] = allgather
-        print(json.dumps(line), flush=True)
+        emit_result(line)
     if pg is not None:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -436,8 +436,15 @@ def time_allgather(args, opt, one_step, device, P, ws):
 
 
 def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
-    """Same metric through the public API, gradients copied from pinned host memory each step
-    and the step's result (norm, found_inf, scale) read back to the host each step."""
+    """Same metric through the public API with host-resident inputs: every step's gradients are
+    copied from pinned host memory, and every step's result (norm, found_inf, scale) is read back
+    to the host before the next step starts.
+
+    The host-to-device copy of step k+1 runs on a copy stream into a device staging buffer while
+    step k computes (one staging buffer: the copy waits until the previous staging contents were
+    moved into the gradient tensors).  The first step's copy happens before the timed region and
+    one extra copy (for the step after the last) inside it, so the region holds exactly one copy
+    per timed step."""
     from minigpt_train_infra_b200 import clip_grad_norm_
     steps = max(2, min(args.steps, args.e2e_steps))
     if pg is not None:
@@ -446,14 +453,29 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
     host = [torch.empty(g.shape, dtype=g.dtype, pin_memory=True) for g in grads]
     for h, g in zip(host, grads):
         h.copy_(g)
+    staging = [torch.empty_like(g) for g in grads]
     res_host = torch.empty(3, dtype=torch.float32, pin_memory=True)
     h2d = sum(g.numel() * g.element_size() for g in grads)
     if pg is not None:
         h2d *= torch.distributed.get_world_size()
+    main = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device)
+    staged = torch.cuda.Event()
+    free = torch.cuda.Event()
+
+    def h2d_async():
+        copy.wait_event(free)
+        with torch.cuda.stream(copy):
+            for st, h in zip(staging, host):
+                st.copy_(h, non_blocking=True)
+        staged.record(copy)
 
     def step():
-        for g, h in zip(grads, host):
-            g.copy_(h, non_blocking=True)
+        main.wait_event(staged)
+        for g, st in zip(grads, staging):
+            g.copy_(st, non_blocking=True)
+        free.record(main)
+        h2d_async()  # the next step's inputs, overlapping this step's kernels
         scaler.unscale_(opt)
         norm = clip_grad_norm_(step_params, CLIP)
         found = next(iter(scaler._per_optimizer_states[id(opt)]["found_inf_per_device"].values()))
@@ -461,8 +483,10 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
         res = torch.stack([norm.float(), found.float(), scaler._scale.float()])
         scaler.update()
         res_host.copy_(res, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        main.synchronize()
 
+    free.record(main)
+    h2d_async()
     step()
     if pg is not None:
         torch.distributed.barrier()
@@ -472,6 +496,7 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
     t0.record()
     for _ in range(steps):
         step()
+    main.wait_event(staged)  # the extra copy issued by the last step is inside the region too
     t1.record()
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
@@ -479,12 +504,65 @@ def run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg):
         t = torch.tensor([ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    del host
+    del host, staging
     return {"value": round(P * steps / (ms / 1e3) / 1e9, 3), "unit": "Gparams/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": 12 * (torch.distributed.get_world_size() if pg else 1),
-            "steps": steps,
-            "ms_per_step": round(ms / steps, 3)}
+            "steps": steps, "ms_per_step": round(ms / steps, 3),
+            "pipelining": "step k+1's host-to-device copy overlaps step k's kernels"}
+
+
+def run_torch_cuda(args) -> None:
+    """torch's own CUDA path for the same workload, as the reference runs it on a GPU
+    (train.py:359-370 with fused=True: fp32 params and grads, AdamW(fused=True), GradScaler,
+    clip_grad_norm_).  An extra measurement for comparison, not the reference arm."""
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    name = args.workload
+    shape_list = workloads.shapes(name)
+    P = workloads.n_params(name)
+    scale = SCALES.get(name, 2.0 ** 16)
+    std = GRAD_STD.get(name, 1e-3)
+    params = [torch.nn.Parameter(torch.empty(s, device=device)) for _, s, _ in shape_list]
+    for i, p in enumerate(params):
+        fill_seeded(p.data, 1000 + i, 0.02)
+        g = torch.empty_like(p)
+        fill_seeded(g, 7000 + i, std * scale)
+        p.grad = g
+    groups = [{"params": [p for p, (_, _, g) in zip(params, shape_list) if g == 0],
+               "weight_decay": WD},
+              {"params": [p for p, (_, _, g) in zip(params, shape_list) if g == 1],
+               "weight_decay": 0.0}]
+    groups = [g for g in groups if g["params"]]
+    opt = torch.optim.AdamW(groups, lr=LR, betas=BETAS, eps=EPS, fused=True)
+    scaler = torch.amp.GradScaler("cuda", init_scale=scale)
+    scaler.scale(torch.ones((), device=device))
+
+    def one_step():
+        scaler.unscale_(opt)
+        torch.nn.utils.clip_grad_norm_(params, CLIP)
+        scaler.step(opt)
+        scaler.update()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    emit_result({"metric": METRIC, "impl": "torch-cuda", "value": round(P / (ms / 1e3) / 1e9, 3),
+                 "unit": "Gparams/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                 "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32",
+                 "config": {"workload": name, "params": P,
+                            "path": f"torch {torch.__version__} AdamW(fused=True) + GradScaler + "
+                                    "clip_grad_norm_, fp32 params and grads"}})
 
 
 def run_reference(args) -> None:
@@ -510,16 +588,36 @@ def run_reference(args) -> None:
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
-    print(json.dumps(line), flush=True)
+    emit_result(line)
+
+
+_RESULT_FD = None
+
+
+def emit_result(line: dict) -> None:
+    """Write the one result line to the real stdout (everything else goes to stderr)."""
+    data = (json.dumps(line) + "\n").encode()
+    fd = _RESULT_FD if _RESULT_FD is not None else 1
+    os.write(fd, data)
+
+
+def _stdout_to_stderr() -> None:
+    """Libraries (NCCL's version banner, for one) print to stdout; keep stdout for the result
+    line only by pointing file descriptor 1 at stderr and remembering the original."""
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
 
 
 def main() -> None:
+    _stdout_to_stderr()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="qwen3_8b", choices=sorted(workloads.WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "torch-cuda"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -528,6 +626,8 @@ def main() -> None:
         log("note: fewer than 3 warm-up steps")
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "torch-cuda":
+        run_torch_cuda(args)
     else:
         run_ours(args)
 

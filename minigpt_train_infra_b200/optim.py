@@ -101,7 +101,12 @@ class FusedAdamW(torch.optim.Optimizer):
         self._store: _FlatStore | None = None
         self._plans: list[ChunkPlan] | None = None
         self._plan_key: tuple | None = None
+        # the plans of the two most recent pointer sets, so a loop that alternates between two
+        # gradient buffers (double-buffered copies or reductions) never re-plans
+        self._plan_cache: dict[tuple, tuple] = {}
         self._pending: GradStats | None = None
+        self._active_ids: frozenset | None = None
+        self.state = _TrackedState(self.state)
         _REGISTRY.add(self)
 
     # ------------------------------------------------------------------------------------
@@ -110,6 +115,7 @@ class FusedAdamW(torch.optim.Optimizer):
 
     def __setstate__(self, state: dict[str, Any]) -> None:
         super().__setstate__(state)
+        self.state = _TrackedState(self.state)
         for group in self.param_groups:
             group.setdefault("amsgrad", False)
             group.setdefault("maximize", False)
@@ -202,6 +208,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self.state.update(foreign)
         self._plans = None
         self._plan_key = None
+        self._plan_cache.clear()
         self._sync_state(force=True)
         for post_hook in self._optimizer_load_state_dict_post_hooks.values():
             post_hook(self)
@@ -217,7 +224,9 @@ class FusedAdamW(torch.optim.Optimizer):
         store = self._store
         device = store.device if store is not None else torch.device("cuda",
                                                                      torch.cuda.current_device())
-        out = torch.zeros(2, dtype=torch.float32, device=device)
+        # [found_inf, norm]; the statistics kernels write both, so no fill is needed
+        out = torch.empty(2, dtype=torch.float32, device=device) if plans else \
+            torch.zeros(2, dtype=torch.float32, device=device)
         if plans:
             stream = stream_ptr(device)
             ls = None
@@ -239,8 +248,12 @@ class FusedAdamW(torch.optim.Optimizer):
         return self._pending
 
     def _owns_exactly(self, params: list[torch.Tensor]) -> bool:
-        mine = {id(p) for g in self.param_groups for p in g["params"] if p.grad is not None}
         theirs = {id(p) for p in params if p.grad is not None}
+        if self._pending is not None and self._active_ids is not None:
+            # the statistics pass of this iteration just matched the plan to these gradients
+            mine = self._active_ids
+        else:
+            mine = {id(p) for g in self.param_groups for p in g["params"] if p.grad is not None}
         return mine == theirs
 
     def set_master_(self, param: torch.Tensor, master: torch.Tensor) -> None:
@@ -279,42 +292,87 @@ class FusedAdamW(torch.optim.Optimizer):
     def _all_params(self) -> list[torch.Tensor]:
         return [p for g in self.param_groups for p in g["params"]]
 
+    def add_param_group(self, param_group: dict[str, Any]) -> None:
+        super().add_param_group(param_group)
+        if getattr(self, "_store", None) is not None:
+            # re-home every parameter's state in new flat buffers that include the new group
+            old = self._store
+            self._sync_state()
+            new = _FlatStore(self._all_params())
+            index = {id(p): i for i, p in enumerate(new.params)}
+            for slot, p in enumerate(old.params):
+                if p in self.state:
+                    new.ingest(index[id(p)], old.views[slot])
+                    self.state[p] = new.views[index[id(p)]]
+            self._store = new
+            self._plans = None
+            self._plan_key = None
+            self._plan_cache.clear()
+
     def _ensure_store(self) -> "_FlatStore":
         if self._store is None:
             self._store = _FlatStore(self._all_params())
         return self._store
+
+    def _tracked_state(self) -> "_TrackedState":
+        st = self.state
+        if not isinstance(st, _TrackedState):
+            st = _TrackedState(st)
+            self.state = st
+        return st
 
     def _sync_state(self, force: bool = False) -> None:
         """Make every ``self.state[p]`` entry a view into the flat buffers.
 
         Entries written from outside (``load_state_dict`` above, or a loader that assigns
         ``optimizer.state[p] = {...}`` such as the reference's ``optim.py:242-251``) are copied
-        into the flat buffers with their values cast to fp32.
+        into the flat buffers with their values cast to fp32.  The state mapping records its own
+        mutations, so an unchanged mapping costs nothing here.
         """
+        st = self._tracked_state()
+        if not st.dirty and not force:
+            return
         if not self._all_params():
             return
         store = self._ensure_store()
         for slot, p in enumerate(store.params):
-            cur = self.state.get(p)
+            cur = st.get(p)
             own = store.views[slot]
             if cur is own:
                 continue
             if cur:
                 store.ingest(slot, cur)
-                self.state[p] = own
+                st[p] = own
             elif force:
-                self.state.pop(p, None)
+                st.pop(p, None)
+        st.dirty = False
 
     def _prepare(self) -> list[ChunkPlan] | None:
-        """Refresh state views and the device plans; returns None when no grads exist."""
-        params = self._all_params()
-        if not params:
+        """Refresh state views and the device plans; returns None when no grads exist.
+
+        Steady state (same gradient and parameter tensors as last step, state untouched) is one
+        pass over the parameters reading their data pointers.
+        """
+        if self._store is None and not self._all_params():
             return None
         store = self._ensure_store()
         self._sync_state()
+        params = store.params
+        grads = [p.grad for p in params]
+        if any(g is None for g in grads):
+            key = None
+        else:
+            key = (tuple(map(_data_ptr, grads)), tuple(map(_data_ptr, params)),
+                   tuple(g.dtype for g in grads))
+            if key == self._plan_key:
+                return self._plans
+            hit = self._plan_cache.get(key)
+            if hit is not None:
+                self._plans, self._active_ids = hit
+                self._plan_key = key
+                return self._plans
         active = []
-        for slot, p in enumerate(store.params):
-            g = p.grad
+        for slot, (p, g) in enumerate(zip(params, grads)):
             if g is None:
                 continue
             if g.is_sparse:
@@ -322,13 +380,24 @@ class FusedAdamW(torch.optim.Optimizer):
             active.append((slot, p, g))
         if not active:
             return None
-        key = tuple((slot, g.data_ptr(), p.data_ptr(), g.dtype) for slot, p, g in active)
+        if key is None:
+            key = (tuple(g.data_ptr() for _, _, g in active),
+                   tuple(p.data_ptr() for _, p, _ in active),
+                   tuple(g.dtype for _, _, g in active), tuple(s for s, _, _ in active))
         if key != self._plan_key:
-            self._plans = self._build_plans(active)
+            hit = self._plan_cache.get(key)
+            if hit is None:
+                hit = (self._build_plans(active), frozenset(id(p) for _, p, _ in active))
+                if len(self._plan_cache) >= 2:
+                    self._plan_cache.pop(next(iter(self._plan_cache)))
+                self._plan_cache[key] = hit
+            self._plans, self._active_ids = hit
             self._plan_key = key
+        st = self._tracked_state()
         for slot, p, _ in active:
-            if p not in self.state or self.state[p] is not store.views[slot]:
-                self.state[p] = store.views[slot]
+            if st.get(p) is not store.views[slot]:
+                st[p] = store.views[slot]
+        st.dirty = False
         return self._plans
 
     def _build_plans(self, active) -> list[ChunkPlan]:
@@ -432,6 +501,53 @@ class _FlatStore:
 
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
+
+
+_data_ptr = torch.Tensor.data_ptr
+
+
+class _TrackedState(defaultdict):
+    """``optimizer.state`` that remembers whether anyone changed it since the optimizer last
+    reconciled it with its flat buffers (torch keeps a plain ``defaultdict(dict)`` here)."""
+
+    def __init__(self, *args):
+        super().__init__(dict, *args)
+        self.dirty = True
+
+    def __reduce__(self):
+        return (dict, (dict(self),))
+
+    def __missing__(self, key):
+        self.dirty = True
+        return super().__missing__(key)
+
+    def __setitem__(self, key, value):
+        self.dirty = True
+        super().__setitem__(key, value)
+
+    def __delitem__(self, key):
+        self.dirty = True
+        super().__delitem__(key)
+
+    def clear(self):
+        self.dirty = True
+        super().clear()
+
+    def pop(self, *args):
+        self.dirty = True
+        return super().pop(*args)
+
+    def popitem(self):
+        self.dirty = True
+        return super().popitem()
+
+    def update(self, *args, **kwargs):
+        self.dirty = True
+        super().update(*args, **kwargs)
+
+    def setdefault(self, key, default=None):
+        self.dirty = True
+        return super().setdefault(key, default)
 
 
 def fused_optimizers() -> list:

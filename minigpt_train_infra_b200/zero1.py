@@ -303,7 +303,7 @@ class ZeroAdamW(torch.optim.Optimizer):
         self._adopt_grads()
         if loss_scale is not None:
             loss_scale = loss_scale.to(device=self.device, dtype=torch.float32)
-        out = torch.zeros(2, dtype=torch.float32, device=self.device)
+        out = torch.empty(2, dtype=torch.float32, device=self.device)  # finalize writes both
         self._kernels.grad_stats(self._plan, loss_scale, self.exch_local)
         if self.world_size > 1:
             dist.all_gather_into_tensor(self.exch_all, self.exch_local, group=self.pg)
