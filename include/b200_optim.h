@@ -201,6 +201,56 @@ int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk
                    float max_norm, float* clip_coef_out, void* workspace, void* stream);
 
 /* ---------------------------------------------------------------------------------------- */
+/* Peer memory and fused collectives (ZeRO-1 over the GPUs of one node)                        */
+/* No counterpart in the reference, which has no data-parallel training path; they replace the */
+/* NCCL reduce-scatter and all-gather a ZeRO-1 trainer would issue around the step.            */
+/* Peer buffers use legacy CUDA IPC (cudaMalloc + cudaIpcGetMemHandle / OpenMemHandle): plain  */
+/* loads and stores over NVLink, no multicast objects.                                        */
+/* ---------------------------------------------------------------------------------------- */
+
+#define B2O_IPC_HANDLE_BYTES 64
+#define B2O_MAX_PEERS 8
+
+/* Allocate `bytes` of device memory on the current device that other processes may map. */
+int b2o_peer_alloc(size_t bytes, void** ptr_out);
+/* Free memory from b2o_peer_alloc (after every peer closed its mapping). */
+int b2o_peer_free(void* ptr);
+/* Write the 64-byte IPC handle of a b2o_peer_alloc allocation to `handle_out` (host). */
+int b2o_peer_export(void* ptr, void* handle_out);
+/* Map another process's allocation from its 64-byte handle (host); *ptr_out is its base. */
+int b2o_peer_import(const void* handle, void** ptr_out);
+/* Unmap an imported allocation. */
+int b2o_peer_close(void* ptr);
+
+/* Reduce-scatter of bf16 gradients fused with the statistics pass.  `peer_grads` (host array
+ * of n_ranks device pointers, index = rank) holds the base address of every rank's flat
+ * gradient buffer as mapped in this process; `my_grad_base` is this rank's own base.  For every
+ * element of the table (this rank's shard): g = bf16(scale_factor * sum over ranks in rank
+ * order of float(grad_r)), accumulated in fp32 and written in place into this rank's buffer;
+ * then the same per-chunk sums of squares and non-finite flag as b2o_grad_stats (flags
+ * B2O_STATS_CLEAR only; finalize with b2o_finalize_norm after exchanging `exch`).  Every rank
+ * must have finished writing its gradients before any rank starts, and no rank may overwrite its
+ * gradients before every rank has finished (order both with a collective on `stream`). */
+int b2o_reduce_scatter_stats(const void* const* peer_grads, int32_t n_ranks,
+                             const void* my_grad_base, float scale_factor,
+                             const b2o_tensor* tensors, int32_t n_tensors,
+                             const b2o_chunk* chunks, int64_t n_chunks, int32_t n_slots,
+                             const float* loss_scale, void* workspace, double* exch,
+                             void* stream);
+
+/* b2o_adamw_step for bf16 parameters that also stores every updated bf16 value into the
+ * parameter buffer of each other rank (`peer_params`, host array of n_ranks bases as mapped in
+ * this process, index = rank; `my_param_base` is this rank's own base): the ZeRO-1 all-gather of
+ * the updated shards fused into the update.  Order it after every rank stopped reading its
+ * parameters and before any rank reads them again (a collective on `stream` on both sides). */
+int b2o_adamw_step_bcast(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk* chunks,
+                         int64_t n_chunks, const b2o_group* groups, int32_t n_groups,
+                         int32_t grad_dtype, float* steps, const float* found_inf,
+                         const float* loss_scale, const float* norm, float max_norm,
+                         void* const* peer_params, int32_t n_ranks, int32_t my_rank,
+                         const void* my_param_base, void* workspace, void* stream);
+
+/* ---------------------------------------------------------------------------------------- */
 /* Loss-scale update                                                                         */
 /* Replaces torch._amp_update_scale_ (torch/amp/grad_scaler.py:549).                          */
 /* ---------------------------------------------------------------------------------------- */

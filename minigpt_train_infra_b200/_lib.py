@@ -70,7 +70,24 @@ SIGNATURES = {
     "b2o_adamw_step": (ctypes.c_int, [_P, _I32, _P, _I64, _P, _I32, _I32, _I32, _P, _P, _P, _P,
                                       _F32, _P, _P, _P]),
     "b2o_scaler_update": (ctypes.c_int, [_P, _P, _P, _F64, _F64, _I32, _P]),
+    "b2o_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, _P]),
+    "b2o_peer_free": (ctypes.c_int, [_P]),
+    "b2o_peer_export": (ctypes.c_int, [_P, _P]),
+    "b2o_peer_import": (ctypes.c_int, [_P, _P]),
+    "b2o_peer_close": (ctypes.c_int, [_P]),
+    "b2o_reduce_scatter_stats": (ctypes.c_int, [_P, _I32, _P, _F32, _P, _I32, _P, _I64, _I32, _P,
+                                                _P, _P, _P]),
+    "b2o_adamw_step_bcast": (ctypes.c_int, [_P, _I32, _P, _I64, _P, _I32, _I32, _P, _P, _P, _P,
+                                            _F32, _P, _I32, _I32, _P, _P, _P]),
 }
+
+IPC_HANDLE_BYTES = 64
+MAX_PEERS = 8
+
+
+def ptr_array(ptrs) -> ctypes.Array:
+    """A host array of device pointers for the entry points that take one per rank."""
+    return (ctypes.c_void_p * len(ptrs))(*ptrs)
 
 _lock = threading.Lock()
 _handle: ctypes.CDLL | None = None

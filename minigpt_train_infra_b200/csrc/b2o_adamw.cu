@@ -91,13 +91,22 @@ __device__ __forceinline__ float clip_coefficient(float norm, float max_norm) {
 #define B2O_ADAMW_SCHED 1
 #endif
 
-template <class G, bool BF16_PARAM, int Q>
+// Where the updated bf16 parameters also go when the ZeRO-1 all-gather is fused into the
+// update: every other rank's copy of the flat parameter buffer (index = rank).
+struct Broadcast {
+  PeerPtrs peers;
+  const char* my_base;
+  int n_ranks;
+  int my_rank;
+};
+
+template <class G, bool BF16_PARAM, int Q, bool BCAST = false>
 __global__ void __launch_bounds__(kThreads, B2O_ADAMW_MIN_CTAS)
 adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
              const b2o_chunk* __restrict__ chunks, int64_t n_chunks, GroupArgs groups,
              float* __restrict__ steps, const float* __restrict__ found_inf,
              const float* __restrict__ loss_scale, const float* __restrict__ norm_p,
-             float max_norm, float* clip_coef_out, Workspace ws) {
+             float max_norm, float* clip_coef_out, Workspace ws, Broadcast bc = Broadcast{}) {
   if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step: no traffic at all
   __shared__ int is_last;
   const float inv = inv_scale_of(loss_scale);
@@ -202,6 +211,13 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
               pq.x = pack_bf16x2(wf[0], wf[1]);
               pq.y = pack_bf16x2(wf[2], wf[3]);
               __stcs(reinterpret_cast<uint2*>(pp + e), pq);
+              if (BCAST) {
+                const int64_t byte = reinterpret_cast<const char*>(pp + e) - bc.my_base;
+#pragma unroll
+                for (int r = 0; r < B2O_MAX_PEERS; ++r)
+                  if (r < bc.n_ranks && r != bc.my_rank)
+                    __stcs(reinterpret_cast<uint2*>(bc.peers.p[r] + byte), pq);
+              }
             }
           }
         }
@@ -216,7 +232,15 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
       wp[e] = w;
       mp[e] = m;
       vp[e] = v;
-      if (BF16_PARAM) pp[e] = to_bf16_bits(w);
+      if (BF16_PARAM) {
+        const uint16_t b = to_bf16_bits(w);
+        pp[e] = b;
+        if (BCAST) {
+          const int64_t byte = reinterpret_cast<const char*>(pp + e) - bc.my_base;
+          for (int r = 0; r < bc.n_ranks; ++r)
+            if (r != bc.my_rank) *reinterpret_cast<uint16_t*>(bc.peers.p[r] + byte) = b;
+        }
+      }
     }
 #if B2O_ADAMW_SCHED == 1
     __syncthreads();  // s_tile[buf ^ 1] is written; every thread moves on together
@@ -228,6 +252,7 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
   }
 
   // Completion ticket; the last CTA advances the step counters after every CTA has read them.
+  if (BCAST) __threadfence_system();  // peer stores performed before the kernel completes
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = atomicAdd(ws.adamw_done, 1u) == gridDim.x - 1;
@@ -257,9 +282,63 @@ int launch_adamw(cudaStream_t s, const b2o_tensor* tensors, int n_tensors,
   return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
 }
 
+int launch_adamw_bcast(cudaStream_t s, const b2o_tensor* tensors, int n_tensors,
+                       const b2o_chunk* chunks, int64_t n_chunks, const GroupArgs& ga,
+                       float* steps, const float* found_inf, const float* loss_scale,
+                       const float* norm, float max_norm, Workspace ws, int grad_dtype,
+                       const Broadcast& bc) {
+  constexpr int Q = B2O_ADAMW_QUADS;
+  if (grad_dtype == B2O_BF16) {
+    const int grid =
+        stream_grid((const void*)adamw_kernel<GradBF16, true, Q, true>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    adamw_kernel<GradBF16, true, Q, true><<<grid, kThreads, 0, s>>>(
+        tensors, n_tensors, chunks, n_chunks, ga, steps, found_inf, loss_scale, norm, max_norm,
+        nullptr, ws, bc);
+  } else {
+    const int grid =
+        stream_grid((const void*)adamw_kernel<GradF32, true, Q, true>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    adamw_kernel<GradF32, true, Q, true><<<grid, kThreads, 0, s>>>(
+        tensors, n_tensors, chunks, n_chunks, ga, steps, found_inf, loss_scale, norm, max_norm,
+        nullptr, ws, bc);
+  }
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}
+
 }  // namespace b2o
 
 using namespace b2o;
+
+extern "C" int b2o_adamw_step_bcast(const b2o_tensor* tensors, int32_t n_tensors,
+                                    const b2o_chunk* chunks, int64_t n_chunks,
+                                    const b2o_group* groups, int32_t n_groups,
+                                    int32_t grad_dtype, float* steps, const float* found_inf,
+                                    const float* loss_scale, const float* norm, float max_norm,
+                                    void* const* peer_params, int32_t n_ranks, int32_t my_rank,
+                                    const void* my_param_base, void* workspace, void* stream) {
+  if (!tensors || !groups || !steps || !workspace || !peer_params || !my_param_base ||
+      n_tensors < 0 || n_chunks < 0)
+    return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS) return B2O_ERR_ARG;
+  if (n_ranks < 1 || n_ranks > B2O_MAX_PEERS || my_rank < 0 || my_rank >= n_ranks)
+    return B2O_ERR_ARG;
+  if (grad_dtype != B2O_BF16 && grad_dtype != B2O_F32) return B2O_ERR_ARG;
+  Broadcast bc{};
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!peer_params[r]) return B2O_ERR_ARG;
+    bc.peers.p[r] = static_cast<char*>(peer_params[r]);
+  }
+  bc.my_base = static_cast<const char*>(my_param_base);
+  bc.n_ranks = n_ranks;
+  bc.my_rank = my_rank;
+  GroupArgs ga{};
+  for (int i = 0; i < n_groups; ++i) ga.g[i] = groups[i];
+  return launch_adamw_bcast(static_cast<cudaStream_t>(stream), tensors, n_tensors, chunks,
+                            n_chunks, ga, steps, found_inf, loss_scale, norm, max_norm,
+                            carve_workspace(workspace, 0), grad_dtype, bc);
+}
 
 extern "C" int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors,
                               const b2o_chunk* chunks, int64_t n_chunks, const b2o_group* groups,

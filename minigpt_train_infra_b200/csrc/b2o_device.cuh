@@ -142,6 +142,12 @@ __device__ __forceinline__ double block_sum(double v, double* scratch) {
   return t;
 }
 
+// Base addresses of every rank's copy of one flat buffer, as mapped in this process (index =
+// rank); passed to kernels by value.
+struct PeerPtrs {
+  char* p[B2O_MAX_PEERS];
+};
+
 // ---------------------------------------------------------------------------------------------
 // Workspace layout (b2o_workspace_bytes): [counters: 8 x uint32][chunk partials: n_chunks x
 // double][exchange: (n_slots + 1) x double].  The counters are the completion tickets of the

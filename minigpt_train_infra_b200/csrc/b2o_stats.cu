@@ -43,6 +43,47 @@ __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slo
   }
 }
 
+// End of a statistics pass, executed by every thread of every CTA after its chunk loop: record
+// the CTA's non-finite flag, take a completion ticket, and let the CTA holding the last ticket
+// fold the chunk partials (per tensor, in chunk order) into exch, then optionally finish the norm.
+__device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __restrict__ tensors,
+                                               int n_tensors, int n_slots, Workspace ws,
+                                               double* exch, int flags, float* found_inf_out,
+                                               float* norm_out, double* scratch, int* is_last_p) {
+  int& is_last = *is_last_p;
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(ws.stats_nonfinite, 1u);
+
+  // Completion ticket: the CTA that takes the last ticket sees every partial.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(ws.stats_done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (flags & B2O_STATS_CLEAR)
+    for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
+  __syncthreads();
+  for (int ti = warp; ti < n_tensors; ti += kWarps) {
+    const b2o_tensor& t = tensors[ti];
+    double sum = 0.0;
+    for (int k = lane; k < t.chunk_count; k += 32) sum += __ldcg(ws.chunk_sums + t.chunk_begin + k);
+    sum = warp_sum(sum);
+    if (lane == 0) exch[t.slot] = sum;
+  }
+  if (threadIdx.x == 0) {
+    const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
+    if (nf) exch[n_slots] += 1.0;
+    *ws.stats_tile = 0u;
+    *ws.stats_done = 0u;
+  }
+  __threadfence();
+  __syncthreads();
+  if (flags & B2O_STATS_FINALIZE)
+    finalize_norm_cta(exch, 1, n_slots, found_inf_out, norm_out, scratch);
+}
+
 // Vectors (8 elements, 16 bytes of bf16) each thread keeps in flight per loop iteration; a
 // build-time knob, the default was measured.
 #ifndef B2O_STATS_UNROLL
@@ -125,37 +166,109 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
 #endif
   }
 
-  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(ws.stats_nonfinite, 1u);
+  stats_epilogue(bad, tensors, n_tensors, n_slots, ws, exch, flags, found_inf_out, norm_out,
+                 scratch, &is_last);
+}
 
-  // Completion ticket: the CTA that takes the last ticket sees every partial.
-  __threadfence();
+// Reduce-scatter of bf16 gradients fused with the statistics pass.  Each element of this rank's
+// shard is summed over every rank's buffer (peer loads over NVLink, fp32, rank order), scaled,
+// rounded to bf16 and written in place; the statistics are taken on the rounded values, i.e. on
+// exactly what the update pass will read.
+template <int U>
+__global__ void __launch_bounds__(kThreads)
+rs_stats_kernel(PeerPtrs peers, int n_ranks, const char* my_base, float scale_factor,
+                const b2o_tensor* __restrict__ tensors, int n_tensors,
+                const b2o_chunk* __restrict__ chunks, int64_t n_chunks, int n_slots,
+                const float* __restrict__ loss_scale, Workspace ws, double* exch) {
+  __shared__ double scratch[kWarps];
+  __shared__ int is_last;
+  __shared__ unsigned int s_tile[2];
+  const float inv = inv_scale_of(loss_scale);
+  bool bad = false;
+  if (threadIdx.x == 0) s_tile[0] = atomicAdd(ws.stats_tile, 1u);
   __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(ws.stats_done, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (flags & B2O_STATS_CLEAR)
-    for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
-  __syncthreads();
-  for (int ti = warp; ti < n_tensors; ti += kWarps) {
-    const b2o_tensor& t = tensors[ti];
-    double sum = 0.0;
-    for (int k = lane; k < t.chunk_count; k += 32) sum += __ldcg(ws.chunk_sums + t.chunk_begin + k);
-    sum = warp_sum(sum);
-    if (lane == 0) exch[t.slot] = sum;
+  int buf = 0;
+  for (int64_t c = s_tile[0]; c < n_chunks;) {
+    if (threadIdx.x == 0) s_tile[buf ^ 1] = atomicAdd(ws.stats_tile, 1u);
+    const b2o_chunk ch = chunks[c];
+    const b2o_tensor& t = tensors[ch.tensor];
+    uint16_t* g = static_cast<uint16_t*>(const_cast<void*>(t.grad));
+    const int64_t off = reinterpret_cast<const char*>(t.grad) - my_base;  // bytes into the buffer
+    double acc = 0.0;
+    const int64_t n = ch.end - ch.begin;
+    int64_t done = 0;
+    if (t.flags & B2O_FLAG_VECTOR) {
+      const int64_t nv = n & ~int64_t(B2O_VEC - 1);
+      done = nv;
+      constexpr int64_t kStride = int64_t(kThreads) * B2O_VEC;
+      for (int64_t i0 = int64_t(threadIdx.x) * B2O_VEC; i0 < nv; i0 += kStride * U) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * kStride;
+          if (i < nv) {
+            const int64_t byte = off + 2 * (ch.begin + i);
+            uint4 v[B2O_MAX_PEERS];
+#pragma unroll
+            for (int r = 0; r < B2O_MAX_PEERS; ++r)
+              if (r < n_ranks) v[r] = ld_stream(reinterpret_cast<const uint4*>(peers.p[r] + byte));
+            float sum[B2O_VEC];
+            {
+              const GradBF16::vec_t v0{v[0]};
+              GradBF16::unpack(v0, sum);
+            }
+#pragma unroll
+            for (int r = 1; r < B2O_MAX_PEERS; ++r) {
+              if (r < n_ranks) {
+                float x[B2O_VEC];
+                const GradBF16::vec_t vr{v[r]};
+                GradBF16::unpack(vr, x);
+#pragma unroll
+                for (int k = 0; k < B2O_VEC; ++k) sum[k] = __fadd_rn(sum[k], x[k]);
+              }
+            }
+            uint4 q;
+            q.x = pack_bf16x2(__fmul_rn(sum[0], scale_factor), __fmul_rn(sum[1], scale_factor));
+            q.y = pack_bf16x2(__fmul_rn(sum[2], scale_factor), __fmul_rn(sum[3], scale_factor));
+            q.z = pack_bf16x2(__fmul_rn(sum[4], scale_factor), __fmul_rn(sum[5], scale_factor));
+            q.w = pack_bf16x2(__fmul_rn(sum[6], scale_factor), __fmul_rn(sum[7], scale_factor));
+            st_stream(reinterpret_cast<uint4*>(g + ch.begin + i), q);
+            const GradBF16::vec_t red{q};
+            bad |= GradBF16::nonfinite(red);
+            float x[B2O_VEC];
+            GradBF16::unpack(red, x);
+            float s2 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < B2O_VEC; ++k) {
+              const float e = __fmul_rn(x[k], inv);
+              s2 = __fmaf_rn(e, e, s2);
+            }
+            acc += (double)s2;
+          }
+        }
+      }
+    }
+    for (int64_t i = done + threadIdx.x; i < n; i += kThreads) {
+      const int64_t byte = off + 2 * (ch.begin + i);
+      float sum = 0.0f;
+      for (int r = 0; r < n_ranks; ++r) {
+        const uint16_t b = *reinterpret_cast<const uint16_t*>(peers.p[r] + byte);
+        const float x = __uint_as_float(static_cast<uint32_t>(b) << 16);
+        sum = r == 0 ? x : __fadd_rn(sum, x);
+      }
+      const uint16_t red = to_bf16_bits(__fmul_rn(sum, scale_factor));
+      g[ch.begin + i] = red;
+      bad |= (red & 0x7f80u) == 0x7f80u;
+      const double u = (double)__fmul_rn(__uint_as_float(static_cast<uint32_t>(red) << 16), inv);
+      acc += u * u;
+    }
+    const double total = block_sum(acc, scratch);
+    if (threadIdx.x == 0) ws.chunk_sums[c] = total;
+    __syncthreads();  // s_tile[buf ^ 1] is written; every thread moves on together
+    buf ^= 1;
+    c = s_tile[buf];
   }
-  if (threadIdx.x == 0) {
-    const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
-    if (nf) exch[n_slots] += 1.0;
-    *ws.stats_tile = 0u;
-    *ws.stats_done = 0u;
-  }
-  __threadfence();
-  __syncthreads();
-  if (flags & B2O_STATS_FINALIZE)
-    finalize_norm_cta(exch, 1, n_slots, found_inf_out, norm_out, scratch);
+  stats_epilogue(bad, tensors, n_tensors, n_slots, ws, exch, B2O_STATS_CLEAR, nullptr, nullptr,
+                 scratch, &is_last);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -195,6 +308,31 @@ extern "C" int b2o_grad_stats(const b2o_tensor* tensors, int32_t n_tensors,
   } else {
     return B2O_ERR_ARG;
   }
+  return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
+}
+
+extern "C" int b2o_reduce_scatter_stats(const void* const* peer_grads, int32_t n_ranks,
+                                        const void* my_grad_base, float scale_factor,
+                                        const b2o_tensor* tensors, int32_t n_tensors,
+                                        const b2o_chunk* chunks, int64_t n_chunks,
+                                        int32_t n_slots, const float* loss_scale,
+                                        void* workspace, double* exch, void* stream) {
+  if (!peer_grads || n_ranks < 1 || n_ranks > B2O_MAX_PEERS || !my_grad_base || !tensors ||
+      !workspace || n_tensors < 0 || n_chunks < 0 || n_slots < 0)
+    return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  PeerPtrs peers{};
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!peer_grads[r]) return B2O_ERR_ARG;
+    peers.p[r] = static_cast<char*>(const_cast<void*>(peer_grads[r]));
+  }
+  Workspace ws = carve_workspace(workspace, n_chunks);
+  if (!exch) exch = ws.exch;
+  const int grid = stream_grid((const void*)rs_stats_kernel<2>, kThreads, n_chunks);
+  if (grid <= 0) return B2O_ERR_CUDA;
+  rs_stats_kernel<2><<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      peers, n_ranks, static_cast<const char*>(my_grad_base), scale_factor, tensors, n_tensors,
+      chunks, n_chunks, n_slots, loss_scale, ws, exch);
   return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
 }
 

@@ -22,6 +22,19 @@ and the step kernels of this package:
 ``defer_param_gather=True`` leaves step (5) to an explicit :meth:`gather_params` call (for a
 trainer that overlaps it with the next forward pass, or a benchmark that times it separately).
 
+Fused collectives over peer memory (``peer_memory=True``, bf16 parameters): the flat buffers are
+allocated so every rank maps every other rank's (``peer.py``, legacy CUDA IPC), and
+
+* ``reduce_grads=True`` -- each rank's ``flat_grad`` holds its own (unreduced) gradients; the
+  statistics pass becomes one kernel that reads this rank's shard range from every rank's buffer
+  over NVLink, sums in fp32 in rank order, applies ``1/world_size`` (``grad_average``), writes the
+  bf16 result in place and takes the statistics on it (``b2o_reduce_scatter_stats``): the
+  gradient reduce-scatter of a data-parallel trainer fused with the norm partials.  Without
+  ``peer_memory`` the same reduction is an NCCL ``reduce_scatter_tensor`` before the pass.
+* the update kernel stores every updated bf16 value into every rank's ``flat_param``
+  (``b2o_adamw_step_bcast``): step (5) fused into step (4), followed by a one-element all-reduce
+  that orders the ranks.
+
 Gradients: ``zero_grad`` zeroes ``flat_grad`` in place and keeps the views (``set_to_none`` has
 no effect: the flat buffer is the gradient storage).  A gradient that autograd allocated
 elsewhere is copied into the flat buffer at the next statistics pass or step.
@@ -122,6 +135,24 @@ class CudaKernels:
                   None if norm is None else norm.data_ptr(), float(max_norm), None,
                   plan.workspace.data_ptr(), stream_ptr(plan.device))
 
+    def reduce_scatter_stats(self, plan: ChunkPlan, peer_grads, n_ranks: int, my_base: int,
+                             scale_factor: float, loss_scale, exch_local: torch.Tensor) -> None:
+        _lib.call("b2o_reduce_scatter_stats", peer_grads, n_ranks, my_base, float(scale_factor),
+                  plan.tensors_ptr, plan.n_tensors, plan.chunks_ptr, plan.n_chunks, plan.n_slots,
+                  None if loss_scale is None else loss_scale.data_ptr(),
+                  plan.workspace.data_ptr(), exch_local.data_ptr(), stream_ptr(plan.device))
+
+    def adamw_bcast(self, plan: ChunkPlan, groups: np.ndarray, steps: torch.Tensor, found_inf,
+                    loss_scale, norm, max_norm: float, peer_params, n_ranks: int, my_rank: int,
+                    my_base: int) -> None:
+        _lib.call("b2o_adamw_step_bcast", plan.tensors_ptr, plan.n_tensors,
+                  plan.update_chunks_ptr, plan.n_update_chunks, _lib.ptr(groups), len(groups),
+                  plan.grad_dtype, steps.data_ptr(),
+                  None if found_inf is None else found_inf.data_ptr(),
+                  None if loss_scale is None else loss_scale.data_ptr(),
+                  None if norm is None else norm.data_ptr(), float(max_norm), peer_params,
+                  n_ranks, my_rank, my_base, plan.workspace.data_ptr(), stream_ptr(plan.device))
+
     def launches_per_step(self) -> int:
         return 3  # stats, finalize, adamw
 
@@ -136,7 +167,8 @@ class ZeroAdamW(torch.optim.Optimizer):
                  maximize: bool = False, foreach: bool | None = None, capturable: bool = False,
                  differentiable: bool = False, fused: bool | None = None,
                  process_group=None, chunk_elems: int | None = DEFAULT_CHUNK_ELEMS,
-                 defer_param_gather: bool = False, _kernels=None):
+                 defer_param_gather: bool = False, peer_memory: bool = False,
+                 reduce_grads: bool = False, grad_average: bool = True, _kernels=None):
         validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
                             chunk_elems)
         defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
@@ -165,14 +197,32 @@ class ZeroAdamW(torch.optim.Optimizer):
         self._kernels = _kernels if _kernels is not None else CudaKernels()
         if _kernels is None and self.device.type != "cuda":
             raise RuntimeError("ZeroAdamW runs on CUDA devices only; there is no CPU path")
+        self.peer_memory = bool(peer_memory) and self.world_size > 1
+        self.reduce_grads = bool(reduce_grads)
+        self.grad_scale_factor = 1.0 / self.world_size if grad_average else 1.0
+        if self.peer_memory and _kernels is not None:
+            raise ValueError("peer_memory needs the CUDA kernels")
+        if self.reduce_grads and self.peer_memory and dtype != torch.bfloat16:
+            raise NotImplementedError("the fused reduce-scatter takes bf16 gradients")
         self.params = plist
         self.n_slots = len(plist)
         self._slot_group = [gi for gi, g in enumerate(self.param_groups) for _ in g["params"]]
         self.geom = ShardGeometry([p.numel() for p in plist], self.world_size, self.rank)
         S = self.geom.shard
         with torch.no_grad():
-            self.flat_param = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
-            self.flat_grad = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
+            self._peer_bufs = []
+            if self.peer_memory:
+                from .peer import PeerBuffer
+                pb = PeerBuffer(self.geom.padded, dtype, self.device, process_group)
+                gb = PeerBuffer(self.geom.padded, dtype, self.device, process_group)
+                self._peer_bufs = [pb, gb]
+                self.flat_param, self.flat_grad = pb.local, gb.local
+                self.flat_param.zero_()
+                self.flat_grad.zero_()
+            else:
+                self.flat_param = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
+                self.flat_grad = torch.zeros(self.geom.padded, dtype=dtype, device=self.device)
+            self._bar = torch.zeros(1, dtype=torch.float32, device=self.device)
             self._grad_views = []
             for p, off in zip(plist, self.geom.offsets):
                 view = self.flat_param[off:off + p.numel()].view(p.shape)
@@ -218,9 +268,29 @@ class ZeroAdamW(torch.optim.Optimizer):
         return self.flat_param[self.geom.lo:self.geom.hi]
 
     def gather_params(self) -> None:
-        """Refresh every rank's ``flat_param`` with the other ranks' updated shards."""
+        """Refresh every rank's ``flat_param`` with the other ranks' updated shards (with
+        ``peer_memory`` the update kernel already stored them; this only orders the ranks)."""
         if self.world_size > 1:
-            dist.all_gather_into_tensor(self.flat_param, self.owned_param_shard(), group=self.pg)
+            if self.peer_memory:
+                self._barrier()
+            else:
+                dist.all_gather_into_tensor(self.flat_param, self.owned_param_shard(),
+                                            group=self.pg)
+
+    def _barrier(self) -> None:
+        """Stream-ordered rendezvous: returns (on the stream) once every rank's earlier work
+        on its stream has completed.  A one-element all-reduce, no host blocking."""
+        dist.all_reduce(self._bar, group=self.pg)
+
+    def close(self) -> None:
+        """Release the peer mappings (with ``peer_memory``); call on every rank."""
+        if self._peer_bufs:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.pg)
+            for b in self._peer_bufs:
+                b.close()
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.pg)
 
     # ------------------------------------------------------------------------------------
     # torch.optim.Optimizer surface
@@ -250,8 +320,16 @@ class ZeroAdamW(torch.optim.Optimizer):
             loss_scale = grad_scale.to(device=self.device, dtype=torch.float32)
         norm = pend.norm if (pend is not None and pend.max_norm is not None) else None
         max_norm = pend.max_norm if norm is not None else 0.0
-        self._kernels.adamw(self._plan, self._group_array(), self.steps, found_inf, loss_scale,
-                            norm, max_norm)
+        if self.peer_memory:
+            # the update stores every new bf16 value into every rank's parameter buffer; the
+            # norm exchange before it already ordered all ranks past their backward passes
+            pb = self._peer_bufs[0]
+            self._kernels.adamw_bcast(self._plan, self._group_array(), self.steps, found_inf,
+                                      loss_scale, norm, max_norm, pb.ptr_array, self.world_size,
+                                      self.rank, pb.local.data_ptr())
+        else:
+            self._kernels.adamw(self._plan, self._group_array(), self.steps, found_inf,
+                                loss_scale, norm, max_norm)
         if not self.defer_param_gather:
             self.gather_params()
         return loss
@@ -304,7 +382,21 @@ class ZeroAdamW(torch.optim.Optimizer):
         if loss_scale is not None:
             loss_scale = loss_scale.to(device=self.device, dtype=torch.float32)
         out = torch.empty(2, dtype=torch.float32, device=self.device)  # finalize writes both
-        self._kernels.grad_stats(self._plan, loss_scale, self.exch_local)
+        if self.reduce_grads and self.world_size > 1:
+            if self.peer_memory:
+                gb = self._peer_bufs[1]
+                self._barrier()  # every rank's gradients are complete
+                self._kernels.reduce_scatter_stats(self._plan, gb.ptr_array, self.world_size,
+                                                   gb.local.data_ptr(), self.grad_scale_factor,
+                                                   loss_scale, self.exch_local)
+            else:
+                shard = self.flat_grad[self.geom.lo:self.geom.hi]
+                dist.reduce_scatter_tensor(shard, self.flat_grad, group=self.pg)
+                if self.grad_scale_factor != 1.0:
+                    shard.mul_(self.grad_scale_factor)
+                self._kernels.grad_stats(self._plan, loss_scale, self.exch_local)
+        else:
+            self._kernels.grad_stats(self._plan, loss_scale, self.exch_local)
         if self.world_size > 1:
             dist.all_gather_into_tensor(self.exch_all, self.exch_local, group=self.pg)
             exch = self.exch_all

@@ -120,3 +120,102 @@ def test_zero_two_nccl_ranks_match_one_gpu(tmp_path):
         for p, off in zip(opt.params, opt.geom.offsets):
             np.testing.assert_array_equal(z["flat"][off:off + p.numel()],
                                           flat1[off:off + p.numel()])
+
+
+def _local_grads(step, rank, device):
+    """Per-rank gradients (different on every rank), bf16, loss-scaled."""
+    gen = torch.Generator().manual_seed(900 + 17 * step + rank)
+    gs = [(torch.randn(s, generator=gen) * 0.05 * 2.0 ** 14).to(torch.bfloat16) for s in SHAPES]
+    if step == 2 and rank == 1:
+        gs[0][3, 7] = float("nan")
+    return [g.to(device) for g in gs]
+
+
+def _reduced_grads(step, world, device):
+    """bf16(0.5 * (g_0 + g_1 + ...)) summed in fp32 in rank order: the fused kernel's rule."""
+    per_rank = [_local_grads(step, r, "cpu") for r in range(world)]
+    out = []
+    for t in range(len(SHAPES)):
+        acc = per_rank[0][t].float()
+        for r in range(1, world):
+            acc = acc + per_rank[r][t].float()
+        out.append((acc * (1.0 / world)).to(torch.bfloat16).to(device))
+    return out
+
+
+def _dp_worker(rank, world, port, out_dir, peer_memory):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [here, os.path.dirname(here)]
+    import torch.distributed as dist
+    from minigpt_train_infra_b200 import GradScaler, ZeroAdamW, clip_grad_norm_
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=device)
+    try:
+        _, params, groups = _init(device)
+        opt = ZeroAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, peer_memory=peer_memory,
+                        reduce_grads=True)
+        sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+        sc.scale(torch.ones((), device=device))
+        norms = []
+        for s in range(5):
+            for p, g in zip(params, _local_grads(s, rank, device)):
+                p.grad.copy_(g)
+            sc.unscale_(opt)
+            norms.append(float(clip_grad_norm_(params, 1.0)))
+            sc.step(opt)
+            sc.update()
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"dp{rank}.npz"), norms=np.array(norms),
+                 scale=float(sc.get_scale()), flat=opt.flat_param.float().cpu().numpy(),
+                 steps=opt.steps.cpu().numpy())
+        opt.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("peer_memory", [True, False])
+def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_memory):
+    """Two ranks with different local gradients: the fused peer-memory reduce-scatter (or NCCL's)
+    plus the step must equal one GPU stepping on the averaged gradients; with peer memory the
+    updated parameters reach every rank through the fused broadcast."""
+    from minigpt_train_infra_b200 import GradScaler, FusedAdamW, clip_grad_norm_
+    port = 29700 + os.getpid() % 1000 + (0 if peer_memory else 1)
+    mp.start_processes(_dp_worker, args=(2, port, str(tmp_path), peer_memory), nprocs=2,
+                       join=True, start_method="spawn")
+    device = torch.device("cuda", 0)
+    _, params, groups = _init(device)
+    opt = FusedAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+    sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+    sc.scale(torch.ones((), device=device))
+    norms = []
+    for s in range(5):
+        for p, g in zip(params, _reduced_grads(s, 2, device)):
+            p.grad = g
+        sc.unscale_(opt)
+        norms.append(float(clip_grad_norm_(params, 1.0)))
+        sc.step(opt)
+        sc.update()
+    # the flat buffer holds the tensors in param-group order (decay group first)
+    ref_flat = [p.detach().float().cpu().numpy().ravel() for g in groups for p in g["params"]]
+    for r in range(2):
+        z = np.load(tmp_path / f"dp{r}.npz")
+        assert float(z["scale"]) == float(sc.get_scale())
+        for a, b in zip(z["norms"], norms):
+            assert (np.isnan(a) and np.isnan(b)) or abs(a - b) <= 2 * np.spacing(np.float32(b))
+        off = 0
+        for t, w in enumerate(ref_flat):
+            n = w.size
+            got = z["flat"][off:off + n]
+            if peer_memory:
+                np.testing.assert_array_equal(got, w)
+            elif n:
+                # NCCL reduces bf16 in its own order; equal up to bf16 rounding of the sums
+                assert np.max(np.abs(got - w)) <= 2 ** -7 * np.max(np.abs(w)) + 1e-12
+            off += (n + 63) // 64 * 64
