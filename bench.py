@@ -565,6 +565,88 @@ def run_torch_cuda(args) -> None:
                                     "clip_grad_norm_, fp32 params and grads"}})
 
 
+def run_dp_step(args) -> None:
+    """The complete data-parallel ZeRO-1 step, N ranks with different local gradients:
+    gradient reduce-scatter -> statistics -> norm exchange -> AdamW -> bf16 parameter gather,
+    either with NCCL collectives around the kernels (``--dp-step nccl``) or with the fused
+    peer-memory kernels (``--dp-step fused``).  Prints its own JSON line; the driver's default
+    line is run_ours."""
+    import datetime
+    import torch.distributed as dist
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    from minigpt_train_infra_b200 import GradScaler, ZeroAdamW, clip_grad_norm_
+    name = args.workload
+    shape_list = workloads.shapes(name)
+    P = workloads.n_params(name)
+    scale = SCALES.get(name, 2.0 ** 16)
+    std = GRAD_STD.get(name, 1e-3)
+    params, gids = make_model_params(shape_list, device)
+    groups = [{"params": [p for p, g in zip(params, gids) if g == 0], "weight_decay": WD},
+              {"params": [p for p, g in zip(params, gids) if g == 1], "weight_decay": 0.0}]
+    groups = [g for g in groups if g["params"]]
+    fused = args.dp_step == "fused"
+    opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=dist.group.WORLD,
+                    reduce_grads=True, peer_memory=fused)
+    fill_seeded(opt.master, 1 + 101 * rank, 0.02)
+    fill_seeded(opt.exp_avg, 2 + 101 * rank, 1e-3)
+    fill_seeded(opt.exp_avg_sq, 3 + 101 * rank, 1e-6, absval=True)
+    opt.steps.fill_(999.0)
+    with torch.no_grad():
+        opt.owned_param_shard().copy_(opt.master)
+    opt.gather_params()
+    local_grads = torch.empty_like(opt.flat_grad)
+    fill_seeded(local_grads, 7 + 1000 * rank, std * scale)  # this rank's own micro-batch grads
+    scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
+    scaler.scale(torch.ones((), device=device))
+    step_params = opt.managed_params()
+
+    def one_step():
+        opt.flat_grad.copy_(local_grads)  # backward's output: fresh local grads every step
+        scaler.unscale_(opt)
+        clip_grad_norm_(step_params, CLIP)
+        scaler.step(opt)
+        scaler.update()
+
+    def timed(fn, k):
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / k], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        one_step()
+    step_ms = timed(one_step, args.steps)
+    copy_ms = timed(lambda: opt.flat_grad.copy_(local_grads), args.steps)
+    ms = step_ms - copy_ms
+    if rank == 0:
+        emit_result({
+            "metric": "ZeRO-1 data-parallel step incl. grad reduce-scatter and param gather",
+            "impl": f"dp-{args.dp_step}", "value": round(P / (ms / 1e3) / 1e9, 3),
+            "unit": "Gparams/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "dtype": "f32",
+            "config": {"workload": name, "params": P,
+                       "collectives": ("fused peer-memory kernels (reduce-scatter+stats, "
+                                       "AdamW+bf16 broadcast)") if fused else
+                       "NCCL reduce_scatter_tensor + all_gather_into_tensor around the kernels",
+                       "note": "the timed loop copies fresh local grads each step (a stand-in "
+                               "for backward); that copy is timed separately and subtracted",
+                       "grad_copy_ms": round(copy_ms, 4)}})
+    opt.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -621,6 +703,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dp-step", choices=["nccl", "fused"], default=None,
+                    help="time the full data-parallel ZeRO-1 step instead (N>1, torchrun)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         log("note: fewer than 3 warm-up steps")
@@ -628,6 +712,8 @@ def main() -> None:
         run_reference(args)
     elif args.impl == "torch-cuda":
         run_torch_cuda(args)
+    elif args.dp_step is not None:
+        run_dp_step(args)
     else:
         run_ours(args)
 
