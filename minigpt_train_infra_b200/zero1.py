@@ -372,6 +372,99 @@ class ZeroAdamW(torch.optim.Optimizer):
                 self.owned_param_shard().copy_(self.master)
         self.gather_params()
 
+    def consolidated_state_dict(self, to_rank: int = 0,
+                                piece_elems: int = 1 << 26) -> dict[str, Any] | None:
+        """The whole optimizer state in FusedAdamW's (torch AdamW's) per-parameter layout, on
+        rank ``to_rank`` (CPU tensors); None on the other ranks.  Call on every rank.
+
+        The owned fp32 ranges are gathered in pieces of ``piece_elems`` elements per rank, so
+        the device holds at most ``world_size * piece_elems`` extra floats at a time.  The
+        result is what the reference's single-file checkpoint stores (``checkpoint.py:41``) and
+        loads into :class:`FusedAdamW` on one GPU or into a ZeroAdamW of any world size
+        (:meth:`load_consolidated_state_dict`).
+        """
+        g = self.geom
+        me = self.rank == to_rank
+        names = ["master", "exp_avg", "exp_avg_sq"]
+        full = {k: torch.empty(g.padded, dtype=torch.float32) for k in names} if me else None
+        for k in names:
+            local = getattr(self, k).detach()
+            if local.dtype != torch.float32:
+                local = local.float()
+            for a in range(0, g.shard, piece_elems):
+                b = min(a + piece_elems, g.shard)
+                piece = local[a:b].contiguous()
+                if self.world_size == 1:
+                    parts = [piece]
+                else:
+                    parts = [torch.empty_like(piece) for _ in range(self.world_size)] if me \
+                        else None
+                    dist.gather(piece, parts, dst=to_rank, group=self.pg)
+                if me:
+                    for r, part in enumerate(parts):
+                        full[k][r * g.shard + a:r * g.shard + b].copy_(part.cpu())
+        steps = self.steps.detach().cpu()
+        if not me:
+            return None
+        state = {}
+        groups = []
+        slot = 0
+        for gi, grp in enumerate(self.param_groups):
+            packed = {k: v for k, v in grp.items() if k != "params"}
+            packed["params"] = list(range(slot, slot + len(grp["params"])))
+            groups.append(packed)
+            for p in grp["params"]:
+                off, n = g.offsets[slot], g.numels[slot]
+                st = {"step": steps[slot].clone(),
+                      "exp_avg": full["exp_avg"][off:off + n].view(p.shape),
+                      "exp_avg_sq": full["exp_avg_sq"][off:off + n].view(p.shape)}
+                if self.flat_param.dtype == torch.bfloat16:
+                    st["master_param"] = full["master"][off:off + n].view(p.shape)
+                state[slot] = st
+                slot += 1
+        return {"state": state, "param_groups": groups}
+
+    def load_consolidated_state_dict(self, state_dict: dict[str, Any]) -> None:
+        """Take this rank's range from a per-parameter state dict (from
+        :meth:`consolidated_state_dict` at any world size, from ``FusedAdamW.state_dict()`` or
+        from ``torch.optim.AdamW.state_dict()``).  Call on every rank with the same dict."""
+        g = self.geom
+        saved_groups = state_dict["param_groups"]
+        if len(saved_groups) != len(self.param_groups) or any(
+                len(a["params"]) != len(b["params"])
+                for a, b in zip(saved_groups, self.param_groups)):
+            raise ValueError("state dict groups do not match this optimizer's parameter groups")
+        for grp, saved in zip(self.param_groups, saved_groups):
+            for k, v in saved.items():
+                if k != "params":
+                    grp[k] = v
+        ids = [i for grp in saved_groups for i in grp["params"]]
+        bf16 = self.flat_param.dtype == torch.bfloat16
+        with torch.no_grad():
+            for slot, sid in enumerate(ids):
+                st = state_dict["state"].get(sid)
+                off, n = g.offsets[slot], g.numels[slot]
+                lo, hi = max(off, g.lo), min(off + n, g.hi)
+                if not st:
+                    continue
+                if "step" in st:
+                    v = st["step"]
+                    self.steps[slot] = float(v.item() if isinstance(v, torch.Tensor) else v)
+                if lo >= hi:
+                    continue
+                a, b = lo - off, hi - off
+                la, lb = lo - g.lo, hi - g.lo
+                for key, dst in (("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+                    if key in st:
+                        dst[la:lb].copy_(st[key].reshape(-1)[a:b])
+                if "master_param" in st:
+                    self.master[la:lb].copy_(st["master_param"].reshape(-1)[a:b])
+                elif bf16:
+                    self.master[la:lb].copy_(self.flat_param[lo:hi])
+            if bf16:
+                self.owned_param_shard().copy_(self.master)
+        self.gather_params()
+
     # ------------------------------------------------------------------------------------
     # GradScaler / clip_grad_norm_ hooks
     # ------------------------------------------------------------------------------------

@@ -241,3 +241,103 @@ def test_rank_failing_before_exchange_gives_bounded_error(tmp_path):
     secs, err = (tmp_path / "rank0.txt").read_text().split("\n", 1)
     assert err.strip(), "the surviving rank returned from the exchange without an error"
     assert float(secs) < 60.0
+
+
+# --------------------------------------------------------------------------------------------
+# consolidated checkpoints and resharding (world 2 -> world 3)
+# --------------------------------------------------------------------------------------------
+
+def _worker_ckpt(rank, world, init_file, out_dir, phase):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [here, os.path.dirname(here)]
+    from zero_oracle_backend import OracleKernels
+    from minigpt_train_infra_b200 import GradScaler, clip_grad_norm_
+    from minigpt_train_infra_b200.zero1 import ZeroAdamW
+    try:
+        w0, params = _make(rank, world, torch.bfloat16, init_file)
+        groups = [{"params": [p for p, s in zip(params, SHAPES) if len(s) >= 2],
+                   "weight_decay": 0.1},
+                  {"params": [p for p, s in zip(params, SHAPES) if len(s) < 2],
+                   "weight_decay": 0.0}]
+        opt = ZeroAdamW(groups, **HP, _kernels=OracleKernels())
+        scaler = GradScaler("cpu", init_scale=2.0 ** 12, growth_interval=3)
+        scaler.scale(torch.ones(()))
+        ck_path = os.path.join(out_dir, "ckpt.pt")
+        if phase == "save":
+            # masters from the fp32 values (the oracle starts from them too)
+            opt.load_consolidated_state_dict({
+                "state": {i: {"master_param": w} for i, w in
+                          enumerate([w0[j] for j in _group_order()])},
+                "param_groups": [{"params": list(range(len(groups[0]["params"])))},
+                                 {"params": list(range(len(groups[0]["params"]),
+                                                       len(SHAPES)))}]})
+            steps = range(0, 3)
+        else:
+            ck = torch.load(ck_path, weights_only=False)
+            opt.load_consolidated_state_dict(ck["optimizer"])
+            scaler.load_state_dict(ck["scaler"])  # bf16 params come from the loaded masters
+            steps = range(3, 5)
+        for step in steps:
+            for p, g in zip(params, _grads(step, torch.bfloat16, 2.0 ** 12)):
+                p.grad = g
+            scaler.unscale_(opt)
+            clip_grad_norm_(opt.managed_params(), 1.0)
+            scaler.step(opt)
+            scaler.update()
+        sd = opt.consolidated_state_dict()
+        if rank == 0:
+            torch.save({"optimizer": sd, "scaler": scaler.state_dict()},
+                       ck_path if phase == "save" else os.path.join(out_dir, "final.pt"))
+        dist.barrier()
+    except Exception:
+        traceback.print_exc()
+        raise
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _group_order():
+    dec = [i for i, s in enumerate(SHAPES) if len(s) >= 2]
+    nod = [i for i, s in enumerate(SHAPES) if len(s) < 2]
+    return dec + nod
+
+
+def _oracle_steps(n_steps):
+    gen = torch.Generator().manual_seed(123)
+    w0 = [torch.randn(s, generator=gen) * 0.02 for s in SHAPES]
+    order = _group_order()
+    groups = [O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.1), O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.0)]
+    states = [O.TensorState(w=w0[i].numpy().copy(), m=np.zeros(SHAPES[i], np.float32),
+                            v=np.zeros(SHAPES[i], np.float32), group=0 if len(SHAPES[i]) >= 2
+                            else 1) for i in order]
+    sc = O.ScalerState(scale=np.float32(2.0 ** 12), growth_interval=3)
+    for step in range(n_steps):
+        gs = _grads(step, torch.bfloat16, 2.0 ** 12)
+        O.optimizer_step(states, [gs[i].float().numpy() for i in order], groups, sc, 1.0)
+    return states, sc
+
+
+@pytest.mark.slow
+def test_consolidated_checkpoint_reshards_from_two_to_three_ranks(tmp_path):
+    mp.spawn(_worker_ckpt, args=(2, str(tmp_path / "rdzv2"), str(tmp_path), "save"),
+             nprocs=2, join=True)
+    ck = torch.load(tmp_path / "ckpt.pt", weights_only=False)["optimizer"]
+    states3, _ = _oracle_steps(3)
+    for slot, st in enumerate(states3):
+        saved = ck["state"][slot]
+        np.testing.assert_array_equal(saved["master_param"].numpy(), st.w)
+        np.testing.assert_array_equal(saved["exp_avg"].numpy(), st.m)
+        np.testing.assert_array_equal(saved["exp_avg_sq"].numpy(), st.v)
+        assert float(saved["step"]) == st.step
+    mp.spawn(_worker_ckpt, args=(3, str(tmp_path / "rdzv3"), str(tmp_path), "load"),
+             nprocs=3, join=True)
+    final = torch.load(tmp_path / "final.pt", weights_only=False)
+    states5, sc5 = _oracle_steps(5)
+    for slot, st in enumerate(states5):
+        saved = final["optimizer"]["state"][slot]
+        np.testing.assert_array_equal(saved["master_param"].numpy(), st.w)
+        np.testing.assert_array_equal(saved["exp_avg"].numpy(), st.m)
+        assert float(saved["step"]) == st.step
+    assert final["scaler"]["scale"] == float(sc5.scale)
