@@ -101,9 +101,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._store: _FlatStore | None = None
         self._plans: list[ChunkPlan] | None = None
         self._plan_key: tuple | None = None
-        # the plans of the two most recent pointer sets, so a loop that alternates between two
-        # gradient buffers (double-buffered copies or reductions) never re-plans
-        self._plan_cache: dict[tuple, tuple] = {}
+        self._grad_key: tuple | None = None
         self._pending: GradStats | None = None
         self._active_ids: frozenset | None = None
         self.state = _TrackedState(self.state)
@@ -208,7 +206,6 @@ class FusedAdamW(torch.optim.Optimizer):
         self.state.update(foreign)
         self._plans = None
         self._plan_key = None
-        self._plan_cache.clear()
         self._sync_state(force=True)
         for post_hook in self._optimizer_load_state_dict_post_hooks.values():
             post_hook(self)
@@ -307,7 +304,6 @@ class FusedAdamW(torch.optim.Optimizer):
             self._store = new
             self._plans = None
             self._plan_key = None
-            self._plan_cache.clear()
 
     def _ensure_store(self) -> "_FlatStore":
         if self._store is None:
@@ -350,8 +346,10 @@ class FusedAdamW(torch.optim.Optimizer):
     def _prepare(self) -> list[ChunkPlan] | None:
         """Refresh state views and the device plans; returns None when no grads exist.
 
-        Steady state (same gradient and parameter tensors as last step, state untouched) is one
-        pass over the parameters reading their data pointers.
+        The plans are keyed by structure (which parameters have gradients, their addresses and
+        gradient dtypes).  New gradient tensors for the same structure -- every step of a loop
+        that calls zero_grad(set_to_none=True) -- only patch the gradient pointers of the
+        device tensor table; the chunk tables are kept.
         """
         if self._store is None and not self._all_params():
             return None
@@ -360,39 +358,32 @@ class FusedAdamW(torch.optim.Optimizer):
         params = store.params
         grads = [p.grad for p in params]
         if any(g is None for g in grads):
-            key = None
+            active = [(slot, p, g) for slot, (p, g) in enumerate(zip(params, grads))
+                      if g is not None]
+            if not active:
+                return None
+            skey = (tuple(p.data_ptr() for _, p, _ in active),
+                    tuple(g.dtype for _, _, g in active), tuple(s for s, _, _ in active))
+            gptr = tuple(g.data_ptr() for _, _, g in active)
+            act_grads = [g for _, _, g in active]
         else:
-            key = (tuple(map(_data_ptr, grads)), tuple(map(_data_ptr, params)),
-                   tuple(g.dtype for g in grads))
-            if key == self._plan_key:
-                return self._plans
-            hit = self._plan_cache.get(key)
-            if hit is not None:
-                self._plans, self._active_ids = hit
-                self._plan_key = key
-                return self._plans
-        active = []
-        for slot, (p, g) in enumerate(zip(params, grads)):
-            if g is None:
-                continue
+            active = None
+            skey = (tuple(map(_data_ptr, params)), tuple(g.dtype for g in grads), None)
+            gptr = tuple(map(_data_ptr, grads))
+            act_grads = grads
+        if skey == self._plan_key:
+            if gptr != self._grad_key:
+                self._refresh_grads(act_grads, gptr)
+            return self._plans
+        if active is None:
+            active = [(slot, p, g) for slot, (p, g) in enumerate(zip(params, grads))]
+        for _, _, g in active:
             if g.is_sparse:
                 raise RuntimeError("FusedAdamW does not support sparse gradients")
-            active.append((slot, p, g))
-        if not active:
-            return None
-        if key is None:
-            key = (tuple(g.data_ptr() for _, _, g in active),
-                   tuple(p.data_ptr() for _, p, _ in active),
-                   tuple(g.dtype for _, _, g in active), tuple(s for s, _, _ in active))
-        if key != self._plan_key:
-            hit = self._plan_cache.get(key)
-            if hit is None:
-                hit = (self._build_plans(active), frozenset(id(p) for _, p, _ in active))
-                if len(self._plan_cache) >= 2:
-                    self._plan_cache.pop(next(iter(self._plan_cache)))
-                self._plan_cache[key] = hit
-            self._plans, self._active_ids = hit
-            self._plan_key = key
+        self._plans = self._build_plans(active)
+        self._plan_key = skey
+        self._grad_key = gptr
+        self._active_ids = frozenset(id(p) for _, p, _ in active)
         st = self._tracked_state()
         for slot, p, _ in active:
             if st.get(p) is not store.views[slot]:
@@ -400,14 +391,26 @@ class FusedAdamW(torch.optim.Optimizer):
         st.dirty = False
         return self._plans
 
+    def _refresh_grads(self, grads: list[torch.Tensor], gptr: tuple) -> None:
+        for g in grads:
+            if not g.is_contiguous():
+                raise RuntimeError("FusedAdamW needs contiguous gradients")
+        ptrs = np.asarray(gptr, dtype=np.uint64)
+        for plan in self._plans:
+            plan.update_grads(ptrs[plan._src])
+        self._grad_refreshes = getattr(self, "_grad_refreshes", 0) + 1
+        self._grad_key = gptr
+
     def _build_plans(self, active) -> list[ChunkPlan]:
+        self._plan_builds = getattr(self, "_plan_builds", 0) + 1
         store = self._store
         gid = {}
         for gi, g in enumerate(self.param_groups):
             for p in g["params"]:
                 gid[id(p)] = gi
         buckets: dict[tuple[int, int], list[Entry]] = {}
-        for slot, p, g in active:
+        srcs: dict[tuple[int, int], list[int]] = {}
+        for k, (slot, p, g) in enumerate(active):
             if g.device != store.device or p.device != store.device:
                 raise RuntimeError("FusedAdamW needs every parameter and gradient on one CUDA "
                                    "device")
@@ -423,10 +426,13 @@ class FusedAdamW(torch.optim.Optimizer):
                           exp_avg_sq=store.exp_avg_sq.data_ptr() + 4 * off, numel=n,
                           group=gid[id(p)], slot=slot)
             buckets.setdefault((gd, pd), []).append(entry)
+            srcs.setdefault((gd, pd), []).append(k)
         plans = []
-        for (gd, pd), entries in buckets.items():
-            plans.append(ChunkPlan(store.device, entries, len(self.param_groups), store.n_slots,
-                                   gd, pd, self._chunk_elems))
+        for key, entries in buckets.items():
+            plan = ChunkPlan(store.device, entries, len(self.param_groups), store.n_slots,
+                             key[0], key[1], self._chunk_elems)
+            plan._src = np.asarray(srcs[key], dtype=np.int64)  # positions in the active list
+            plans.append(plan)
         return plans
 
 

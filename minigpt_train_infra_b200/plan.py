@@ -111,6 +111,19 @@ class ChunkPlan:
         self.table = torch.empty(blob.size, dtype=torch.uint8, device=device)
         self.table.copy_(staging, non_blocking=True)
         self._staging = staging  # kept alive with the plan, so the async copy never races
+        # Gradient pointers change every step in a loop that frees its gradients
+        # (zero_grad(set_to_none=True)); the chunk tables do not depend on them, so only the
+        # tensor entries are patched and re-uploaded (update_grads), through a small ring of
+        # pinned buffers so a pending upload is never overwritten.
+        other = np.ones(n, dtype=bool)
+        for f in ("param", "master", "exp_avg", "exp_avg_sq"):
+            other &= (host_t[f] & np.uint64(15)) == 0
+        self._others_aligned = other
+        self._t_nbytes = host_t.nbytes
+        self._ring = [torch.empty(host_t.nbytes, dtype=torch.uint8).pin_memory()
+                      for _ in range(3)]
+        self._ring_events: list = [None, None, None]
+        self._ring_i = 0
         self.tensors_ptr = self.table.data_ptr()
         self.chunks_ptr = self.table.data_ptr() + t_bytes
         self.update_chunks_ptr = self.table.data_ptr() + t_bytes + s_bytes
@@ -125,6 +138,27 @@ class ChunkPlan:
         # Per-slot exchange vector (n_slots + 1 doubles) inside the workspace.
         exch_off = 64 + 8 * self.n_chunks
         self.exch = self.workspace[exch_off:exch_off + 8 * (n_slots + 1)].view(torch.float64)
+
+    def update_grads(self, grad_ptrs: np.ndarray) -> None:
+        """Point the tensor entries at new gradient tensors (same sizes and dtypes, in entry
+        order) and upload the entries on the current stream, after the kernels already queued."""
+        t = self.host_tensors
+        grad_ptrs = np.asarray(grad_ptrs, dtype=np.uint64)
+        if np.any((grad_ptrs == 0) & (t["numel"] > 0)):
+            raise RuntimeError("null gradient pointer for a non-empty tensor")
+        t["grad"] = grad_ptrs
+        ok = ((grad_ptrs & np.uint64(15)) == 0) & self._others_aligned
+        t["flags"] = np.where(ok, _lib.FLAG_VECTOR, 0).astype(np.int32)
+        i = self._ring_i
+        self._ring_i = (i + 1) % len(self._ring)
+        if self._ring_events[i] is not None:
+            self._ring_events[i].synchronize()
+        buf = self._ring[i]
+        buf.numpy()[:] = t.view(np.uint8)
+        self.table[:self._t_nbytes].copy_(buf, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._ring_events[i] = ev
 
     def vector_fraction(self) -> float:
         """Fraction of elements whose tensor qualifies for the 128-bit path."""
