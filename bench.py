@@ -287,7 +287,7 @@ def run_ours(args) -> None:
         step_params = opt.managed_params()
         params = step_params
     else:
-        opt = FusedAdamW(groups, lr=LR, betas=BETAS, eps=EPS)
+        opt = FusedAdamW(groups, lr=LR, betas=BETAS, eps=EPS, capturable=args.graph)
         seed_state(opt, params)
         grads = make_grads(params, scale, std)
         step_params = params
@@ -316,6 +316,25 @@ def run_ours(args) -> None:
     for _ in range(args.warmup):
         one_step()
     torch.cuda.synchronize()
+    if args.graph and ws == 1:
+        # the whole step captured once; each timed step stages hyper-parameters and replays
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            scaler.unscale_(opt)
+            clip_grad_norm_(step_params, CLIP)
+            scaler.step(opt)
+            scaler.update()
+        torch.cuda.synchronize()
+
+        def one_step(ev=None):  # noqa: F811 -- the timed step becomes a replay
+            if ev is not None:
+                ev[0].record()
+            opt.prepare_replay()
+            graph.replay()
+            if ev is not None:
+                ev[1].record()
+                ev[2].record()
+                ev[3].record()
     if pg is not None:
         torch.distributed.barrier()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
@@ -703,6 +722,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="N=1: capture the step in a CUDA graph and time its replays")
     ap.add_argument("--dp-step", choices=["nccl", "fused"], default=None,
                     help="time the full data-parallel ZeRO-1 step instead (N>1, torchrun)")
     args = ap.parse_args()

@@ -200,6 +200,17 @@ int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk
                    const float* found_inf, const float* loss_scale, const float* norm,
                    float max_norm, float* clip_coef_out, void* workspace, void* stream);
 
+/* b2o_adamw_step with the group hyper-parameters read from device memory (`dev_groups`,
+ * n_groups entries) when the kernel runs, instead of passed by value at launch: a launch
+ * recorded in a CUDA graph then follows learning-rate schedules by rewriting `dev_groups`
+ * between replays.  No counterpart in the reference (torch's AdamW(capturable=True) holds lr in
+ * a device tensor for the same reason). */
+int b2o_adamw_step_dev(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk* chunks,
+                       int64_t n_chunks, const b2o_group* dev_groups, int32_t n_groups,
+                       int32_t grad_dtype, int32_t param_dtype, float* steps,
+                       const float* found_inf, const float* loss_scale, const float* norm,
+                       float max_norm, void* workspace, void* stream);
+
 /* ---------------------------------------------------------------------------------------- */
 /* Peer memory and fused collectives (ZeRO-1 over the GPUs of one node)                        */
 /* No counterpart in the reference, which has no data-parallel training path; they replace the */

@@ -70,6 +70,8 @@ SIGNATURES = {
     "b2o_adamw_step": (ctypes.c_int, [_P, _I32, _P, _I64, _P, _I32, _I32, _I32, _P, _P, _P, _P,
                                       _F32, _P, _P, _P]),
     "b2o_scaler_update": (ctypes.c_int, [_P, _P, _P, _F64, _F64, _I32, _P]),
+    "b2o_adamw_step_dev": (ctypes.c_int, [_P, _I32, _P, _I64, _P, _I32, _I32, _I32, _P, _P, _P,
+                                          _P, _F32, _P, _P]),
     "b2o_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, _P]),
     "b2o_peer_free": (ctypes.c_int, [_P]),
     "b2o_peer_export": (ctypes.c_int, [_P, _P]),

@@ -100,13 +100,14 @@ struct Broadcast {
   int my_rank;
 };
 
-template <class G, bool BF16_PARAM, int Q, bool BCAST = false>
+template <class G, bool BF16_PARAM, int Q, bool BCAST = false, bool DEV_HP = false>
 __global__ void __launch_bounds__(kThreads, B2O_ADAMW_MIN_CTAS)
 adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
              const b2o_chunk* __restrict__ chunks, int64_t n_chunks, GroupArgs groups,
              float* __restrict__ steps, const float* __restrict__ found_inf,
              const float* __restrict__ loss_scale, const float* __restrict__ norm_p,
-             float max_norm, float* clip_coef_out, Workspace ws, Broadcast bc = Broadcast{}) {
+             float max_norm, float* clip_coef_out, Workspace ws, Broadcast bc = Broadcast{},
+             const b2o_group* __restrict__ dev_groups = nullptr) {
   if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step: no traffic at all
   __shared__ int is_last;
   const float inv = inv_scale_of(loss_scale);
@@ -166,7 +167,7 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
       vp = t.exp_avg_sq;
       pp = static_cast<uint16_t*>(t.param);
       flags = t.flags;
-      warp_scalars(groups.g[t.group], steps[t.slot], lane, s);
+      warp_scalars(DEV_HP ? dev_groups[t.group] : groups.g[t.group], steps[t.slot], lane, s);
     }
     const int64_t n = ch.end - ch.begin;
     int64_t done = 0;
@@ -273,12 +274,22 @@ template <class G, bool P>
 int launch_adamw(cudaStream_t s, const b2o_tensor* tensors, int n_tensors,
                  const b2o_chunk* chunks, int64_t n_chunks, const GroupArgs& ga, float* steps,
                  const float* found_inf, const float* loss_scale, const float* norm, float max_norm,
-                 float* coef_out, Workspace ws) {
+                 float* coef_out, Workspace ws, const b2o_group* dev_groups = nullptr) {
   constexpr int Q = B2O_ADAMW_QUADS;
-  const int grid = stream_grid((const void*)adamw_kernel<G, P, Q>, kThreads, n_chunks);
-  if (grid <= 0) return B2O_ERR_CUDA;
-  adamw_kernel<G, P, Q><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks, ga, steps,
-                                                  found_inf, loss_scale, norm, max_norm, coef_out, ws);
+  if (dev_groups) {
+    const int grid =
+        stream_grid((const void*)adamw_kernel<G, P, Q, false, true>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    adamw_kernel<G, P, Q, false, true><<<grid, kThreads, 0, s>>>(
+        tensors, n_tensors, chunks, n_chunks, ga, steps, found_inf, loss_scale, norm, max_norm,
+        coef_out, ws, Broadcast{}, dev_groups);
+  } else {
+    const int grid = stream_grid((const void*)adamw_kernel<G, P, Q>, kThreads, n_chunks);
+    if (grid <= 0) return B2O_ERR_CUDA;
+    adamw_kernel<G, P, Q><<<grid, kThreads, 0, s>>>(tensors, n_tensors, chunks, n_chunks, ga,
+                                                    steps, found_inf, loss_scale, norm, max_norm,
+                                                    coef_out, ws);
+  }
   return cudaGetLastError() == cudaSuccess ? B2O_OK : B2O_ERR_LAUNCH;
 }
 
@@ -372,5 +383,38 @@ extern "C" int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors,
                                                 steps, found_inf, loss_scale, norm, max_norm,
                                                 clip_coef_out, ws);
   }
+  return B2O_ERR_ARG;
+}
+
+extern "C" int b2o_adamw_step_dev(const b2o_tensor* tensors, int32_t n_tensors,
+                                  const b2o_chunk* chunks, int64_t n_chunks,
+                                  const b2o_group* dev_groups, int32_t n_groups,
+                                  int32_t grad_dtype, int32_t param_dtype, float* steps,
+                                  const float* found_inf, const float* loss_scale,
+                                  const float* norm, float max_norm, void* workspace,
+                                  void* stream) {
+  if (!tensors || !dev_groups || !steps || !workspace || n_tensors < 0 || n_chunks < 0)
+    return B2O_ERR_ARG;
+  if (n_chunks > 0 && !chunks) return B2O_ERR_ARG;
+  if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS) return B2O_ERR_ARG;
+  if (param_dtype != B2O_BF16 && param_dtype != B2O_F32) return B2O_ERR_ARG;
+  const GroupArgs ga{};
+  Workspace ws = carve_workspace(workspace, n_chunks);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16p = param_dtype == B2O_BF16;
+  if (grad_dtype == B2O_BF16)
+    return bf16p ? launch_adamw<GradBF16, true>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                                steps, found_inf, loss_scale, norm, max_norm,
+                                                nullptr, ws, dev_groups)
+                 : launch_adamw<GradBF16, false>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                                 steps, found_inf, loss_scale, norm, max_norm,
+                                                 nullptr, ws, dev_groups);
+  if (grad_dtype == B2O_F32)
+    return bf16p ? launch_adamw<GradF32, true>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                               steps, found_inf, loss_scale, norm, max_norm,
+                                               nullptr, ws, dev_groups)
+                 : launch_adamw<GradF32, false>(s, tensors, n_tensors, chunks, n_chunks, ga,
+                                                steps, found_inf, loss_scale, norm, max_norm,
+                                                nullptr, ws, dev_groups);
   return B2O_ERR_ARG;
 }

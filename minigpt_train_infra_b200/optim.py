@@ -25,6 +25,10 @@ What is different underneath:
   so ``param.grad`` still holds the scaled gradients after ``unscale_``;
 * bf16 parameters are refreshed from the fp32 masters by the same kernel.
 
+``capturable=True`` makes the step capturable in a CUDA graph: the update kernel then reads the
+group hyper-parameters from a device array instead of launch arguments, and ``prepare_replay()``
+stages the current lr and gradient pointers before each replay.
+
 CUDA tensors only; there is no CPU path.  Not supported (raise): ``amsgrad``, ``maximize``,
 ``differentiable``, sparse gradients, fp16 parameters.
 """
@@ -102,6 +106,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._plans: list[ChunkPlan] | None = None
         self._plan_key: tuple | None = None
         self._grad_key: tuple | None = None
+        self._hp_dev: torch.Tensor | None = None
         self._pending: GradStats | None = None
         self._active_ids: frozenset | None = None
         self.state = _TrackedState(self.state)
@@ -151,17 +156,68 @@ class FusedAdamW(torch.optim.Optimizer):
             loss_scale = grad_scale.to(device=device, dtype=torch.float32, non_blocking=True)
         norm = pend.norm if (pend is not None and pend.max_norm is not None) else None
         max_norm = pend.max_norm if norm is not None else 0.0
-        groups = self._group_array()
         stream = stream_ptr(device)
+        fi = None if found_inf is None else found_inf.data_ptr()
+        ls = None if loss_scale is None else loss_scale.data_ptr()
+        nm = None if norm is None else norm.data_ptr()
+        if self._capturable():
+            # hyper-parameters from device memory, so a CUDA graph of this step follows lr
+            # schedules; outside a capture they are staged here, before a replay by
+            # prepare_replay()
+            if not torch.cuda.is_current_stream_capturing():
+                self.stage_hyperparams()
+            hp = self._hp_dev
+            for plan in plans:
+                _lib.call("b2o_adamw_step_dev", plan.tensors_ptr, plan.n_tensors,
+                          plan.update_chunks_ptr, plan.n_update_chunks, hp.data_ptr(),
+                          len(self.param_groups), plan.grad_dtype, plan.param_dtype,
+                          store.steps.data_ptr(), fi, ls, nm, float(max_norm),
+                          plan.workspace.data_ptr(), stream)
+            return loss
+        groups = self._group_array()
         for plan in plans:
             _lib.call("b2o_adamw_step", plan.tensors_ptr, plan.n_tensors,
-                      plan.update_chunks_ptr, plan.n_update_chunks, _lib.ptr(groups), len(groups), plan.grad_dtype,
-                      plan.param_dtype, store.steps.data_ptr(),
-                      None if found_inf is None else found_inf.data_ptr(),
-                      None if loss_scale is None else loss_scale.data_ptr(),
-                      None if norm is None else norm.data_ptr(), float(max_norm), None,
-                      plan.workspace.data_ptr(), stream)
+                      plan.update_chunks_ptr, plan.n_update_chunks, _lib.ptr(groups),
+                      len(groups), plan.grad_dtype, plan.param_dtype, store.steps.data_ptr(),
+                      fi, ls, nm, float(max_norm), None, plan.workspace.data_ptr(), stream)
         return loss
+
+    # ------------------------------------------------------------------------------------
+    # CUDA graphs (capturable=True)
+    # ------------------------------------------------------------------------------------
+
+    def _capturable(self) -> bool:
+        return any(g.get("capturable", False) for g in self.param_groups)
+
+    def stage_hyperparams(self) -> None:
+        """Copy every group's lr/betas/eps/weight_decay to the device array the update kernel
+        reads when ``capturable=True`` (ordered on the current stream; no host wait except when
+        a ring buffer from three calls ago has not been consumed yet)."""
+        arr = self._group_array()
+        n = arr.nbytes
+        if self._hp_dev is None or self._hp_dev.numel() != n:
+            dev = self._ensure_store().device
+            self._hp_dev = torch.empty(n, dtype=torch.uint8, device=dev)
+            self._hp_ring = [torch.empty(n, dtype=torch.uint8).pin_memory() for _ in range(3)]
+            self._hp_events = [None, None, None]
+            self._hp_i = 0
+        i = self._hp_i
+        self._hp_i = (i + 1) % 3
+        if self._hp_events[i] is not None:
+            self._hp_events[i].synchronize()
+        self._hp_ring[i].numpy()[:] = arr.view(np.uint8)
+        self._hp_dev.copy_(self._hp_ring[i], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._hp_events[i] = ev
+
+    def prepare_replay(self) -> None:
+        """Before replaying a CUDA graph that captured this optimizer's step: point the device
+        tables at the current gradient tensors and stage the current hyper-parameters."""
+        if not self._capturable():
+            raise RuntimeError("construct the optimizer with capturable=True to replay it")
+        self._prepare()
+        self.stage_hyperparams()
 
     def state_dict(self) -> dict[str, Any]:
         self._sync_state()
@@ -373,8 +429,13 @@ class FusedAdamW(torch.optim.Optimizer):
             act_grads = grads
         if skey == self._plan_key:
             if gptr != self._grad_key:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError("gradient tensors changed since the last step; call "
+                                       "prepare_replay() (or one eager step) before capturing")
                 self._refresh_grads(act_grads, gptr)
             return self._plans
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("run one eager step before capturing the optimizer in a graph")
         if active is None:
             active = [(slot, p, g) for slot, (p, g) in enumerate(zip(params, grads))]
         for _, _, g in active:
