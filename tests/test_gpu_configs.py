@@ -1,0 +1,251 @@
+"""Parity at the full sizes of the benchmark configurations.
+
+At these sizes the reference's own CPU norm is inaccurate (torch accumulates fp32 norms in fp32:
+-4.3% at 2**28 elements), so the checks are: the oracle fed the kernel's own norm must agree bit
+for bit (on every element where the oracle is cheap enough, on seeded samples elsewhere), the
+kernel's norm must be within 2 ulp of an fp64 norm, and size-independent properties must hold
+(skip decisions, loss-scale sequence, step counters, a skipped step leaving every state word
+unchanged).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from minigpt_train_infra_b200 import workloads
+from oracle import adamw_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _fp64_norm(grads, inv_scale: float) -> float:
+    """fp32(sqrt(sum_t fp32(sqrt(sum x^2))^2)) with x = fp32(g * inv_scale), sums in fp64."""
+    norms = []
+    for g in grads:
+        x = (g.float() * inv_scale).double()
+        norms.append(np.float32(math.sqrt(float((x * x).sum()))))
+    return float(O.total_norm(norms))
+
+
+def test_config1_minigpt_fp32_ten_steps_every_element():
+    """Config 1: MiniGPT 6L/384 (76 tensors, 10,770,816 params) in fp32, scaler off, clip 1.0,
+    lr 6e-4, betas (0.9, 0.95), wd 0.1 on 2-D weights; 10 steps, every element checked."""
+    from minigpt_train_infra_b200 import FusedAdamW, clip_grad_norm_
+    shapes = workloads.shapes("minigpt_6l_384")
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    w0 = [torch.randn(s, generator=gen, device=DEV) * 0.02 for _, s, _ in shapes]
+    params = [torch.nn.Parameter(w.clone()) for w in w0]
+    groups = [{"params": [p for p, (_, _, g) in zip(params, shapes) if g == 0],
+               "weight_decay": 0.1},
+              {"params": [p for p, (_, _, g) in zip(params, shapes) if g == 1],
+               "weight_decay": 0.0}]
+    opt = FusedAdamW(groups, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    order = [i for i, (_, _, g) in enumerate(shapes) if g == 0] + \
+            [i for i, (_, _, g) in enumerate(shapes) if g == 1]
+    hp = [O.GroupHP(6e-4, 0.9, 0.95, 1e-8, 0.1), O.GroupHP(6e-4, 0.9, 0.95, 1e-8, 0.0)]
+    states = [O.TensorState(w=w0[i].cpu().numpy(), m=np.zeros(shapes[i][1], np.float32),
+                            v=np.zeros(shapes[i][1], np.float32), group=shapes[i][2])
+              for i in order]
+    for step in range(10):
+        grads = [torch.randn(s, generator=gen, device=DEV) * 0.05 for _, s, _ in shapes]
+        for p, g in zip(params, grads):
+            p.grad = g
+        norm = clip_grad_norm_(params, 1.0)
+        opt.step()
+        g_host = [grads[i].cpu().numpy() for i in order]
+        O.optimizer_step(states, g_host, hp, None, 1.0, norm=np.float32(norm.item()))
+        assert abs(float(norm) - _fp64_norm(grads, 1.0)) <= 2 * np.spacing(np.float32(norm.item()))
+    for k, i in enumerate(order):
+        np.testing.assert_array_equal(params[i].detach().cpu().numpy(), states[k].w)
+        np.testing.assert_array_equal(opt.state[params[i]]["exp_avg"].cpu().numpy(), states[k].m)
+        np.testing.assert_array_equal(opt.state[params[i]]["exp_avg_sq"].cpu().numpy(),
+                                      states[k].v)
+        assert float(opt.state[params[i]]["step"]) == 10.0
+
+
+def test_config2_flat_2_28_sampled():
+    """Config 2: one tensor of 2**28, master~N(0,0.02), m~N(0,1e-3), v=|N(0,1)|*1e-6,
+    grads bf16(N(0,1e-2)*2**16), step 1000, lr 3e-4, betas (0.9,0.95), wd 0.1, clip 1.0."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    n = 1 << 28
+    gen = torch.Generator(device=DEV).manual_seed(2)
+    p = torch.nn.Parameter(torch.empty(n, dtype=torch.bfloat16, device=DEV))
+    opt = FusedAdamW([p], lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    st = opt._ensure_store()
+    opt._sync_state()
+    master = st.master[:n]
+    master.normal_(0, 0.02, generator=gen)
+    st.exp_avg[:n].normal_(0, 1e-3, generator=gen)
+    st.exp_avg_sq[:n].normal_(0, 1, generator=gen).abs_().mul_(1e-6)
+    st.steps.fill_(999.0)
+    with torch.no_grad():
+        p.copy_(master)
+    g = (torch.randn(n, generator=gen, device=DEV) * 1e-2 * 2.0 ** 16).to(torch.bfloat16)
+    p.grad = g
+    idx = torch.randint(0, n, (1 << 20,), generator=gen, device=DEV)
+    w_in, m_in, v_in = master[idx].cpu().numpy(), st.exp_avg[idx].cpu().numpy(), \
+        st.exp_avg_sq[idx].cpu().numpy()
+    g_in = _bits(g[idx])
+    sc = GradScaler("cuda", init_scale=2.0 ** 16)
+    sc.scale(torch.ones((), device=DEV))
+    sc.unscale_(opt)
+    norm = clip_grad_norm_([p], 1.0)
+    sc.step(opt)
+    sc.update()
+    nrm = np.float32(norm.item())
+    assert abs(float(nrm) - _fp64_norm([g], 2.0 ** -16)) <= 2 * np.spacing(nrm)
+    assert float(nrm) > 1.0  # clipping active (norm ~ 1e-2 * sqrt(2**28) ~ 164)
+    s = O.TensorState(w=w_in, m=m_in, v=v_in, step=999.0)
+    O.optimizer_step([s], [O.bf16_bits_to_f32(g_in)], [O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.1)],
+                     O.ScalerState(scale=np.float32(2.0 ** 16)), 1.0, norm=nrm)
+    np.testing.assert_array_equal(master[idx].cpu().numpy(), s.w)
+    np.testing.assert_array_equal(st.exp_avg[idx].cpu().numpy(), s.m)
+    np.testing.assert_array_equal(st.exp_avg_sq[idx].cpu().numpy(), s.v)
+    np.testing.assert_array_equal(_bits(p.detach()[idx]), O.f32_to_bf16_bits(s.w))
+
+
+def test_config3_gpt2_hundred_steps_inf_every_tenth():
+    """Config 3: GPT-2 124M (148 tensors), bf16 grads N(0,1e-3)*2**16 fresh each step, scaler
+    init 2**16 / growth interval 2000 / backoff 0.5, +inf at one seeded element every 10th step,
+    100 steps: 10 skips, scale 2**16 * 0.5**10 = 64, no growth, step counters 90; the 1-D tensors
+    (98 tensors, 121,344 params) are followed by the oracle every step and compared element by
+    element every 25 steps."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    shapes = workloads.shapes("gpt2_124m")
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    w0 = [(torch.randn(s, generator=gen, device=DEV) * 0.02) for _, s, _ in shapes]
+    params = [torch.nn.Parameter(w.to(torch.bfloat16)) for w in w0]
+    groups = [{"params": [p for p, (_, _, g) in zip(params, shapes) if g == 0],
+               "weight_decay": 0.1},
+              {"params": [p for p, (_, _, g) in zip(params, shapes) if g == 1],
+               "weight_decay": 0.0}]
+    opt = FusedAdamW(groups, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+    for p, w in zip(params, w0):
+        opt.set_master_(p, w)
+    sc = GradScaler("cuda", init_scale=2.0 ** 16, growth_interval=2000, backoff_factor=0.5)
+    sc.scale(torch.ones((), device=DEV))
+    small = [i for i, (_, s, _) in enumerate(shapes) if len(s) == 1]
+    hp = [O.GroupHP(6e-4, 0.9, 0.95, 1e-8, 0.1), O.GroupHP(6e-4, 0.9, 0.95, 1e-8, 0.0)]
+    ost = {i: O.TensorState(w=w0[i].cpu().numpy(), m=np.zeros(shapes[i][1], np.float32),
+                            v=np.zeros(shapes[i][1], np.float32), group=1) for i in small}
+    osc = O.ScalerState(scale=np.float32(2.0 ** 16))
+    pick = torch.Generator().manual_seed(33)
+    skips = 0
+    for step in range(100):
+        grads = [(torch.randn(s, generator=gen, device=DEV) * 1e-3 * 2.0 ** 16).to(torch.bfloat16)
+                 for _, s, _ in shapes]
+        if step % 10 == 9:
+            t = int(torch.randint(0, len(shapes), (1,), generator=pick))
+            e = int(torch.randint(0, grads[t].numel(), (1,), generator=pick))
+            grads[t].view(-1)[e] = float("inf")
+        for p, g in zip(params, grads):
+            p.grad = g
+        sc.unscale_(opt)
+        norm = clip_grad_norm_(params, 1.0)
+        found = float(next(iter(sc._per_optimizer_states[id(opt)]["found_inf_per_device"]
+                                .values())))
+        sc.step(opt)
+        sc.update()
+        assert found == (1.0 if step % 10 == 9 else 0.0), step
+        skips += int(found)
+        # the oracle over the 1-D tensors, with the kernel's (global) norm and skip decision
+        if found:
+            osc.scale, osc.tracker = O.scaler_update(osc.scale, osc.tracker, True, 2.0, 0.5, 2000)
+        else:
+            O.optimizer_step([ost[i] for i in small],
+                             [O.bf16_bits_to_f32(_bits(grads[i])) for i in small],
+                             hp, osc, 1.0, norm=np.float32(norm.item()))
+        assert float(osc.scale) == float(sc.get_scale())
+        if step % 25 == 24:
+            for i in small:
+                np.testing.assert_array_equal(opt.state[params[i]]["master_param"].cpu().numpy(),
+                                              ost[i].w)
+                np.testing.assert_array_equal(opt.state[params[i]]["exp_avg_sq"].cpu().numpy(),
+                                              ost[i].v)
+    assert skips == 10
+    assert float(sc.get_scale()) == 2.0 ** 16 * 0.5 ** 10 == 64.0
+    assert int(sc._growth_tracker.item()) == 0
+    assert {float(s["step"]) for s in opt.state.values()} == {90.0}
+
+
+def test_config4_qwen3_1_7b_skip_is_free_and_step_matches():
+    """Config 4 on one GPU: Qwen3-1.7B-shaped (310 tensors, 1,720,574,976 params, ~28 GB of
+    state).  A step whose gradients hold a NaN leaves every state word and every bf16 parameter
+    unchanged; a clean step matches the oracle on seeded samples of every tensor."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    shapes = workloads.shapes("qwen3_1_7b")
+    gen = torch.Generator(device=DEV).manual_seed(4)
+    params = [torch.nn.Parameter(torch.empty(s, dtype=torch.bfloat16, device=DEV))
+              for _, s, _ in shapes]
+    groups = [{"params": [p for p, (_, _, g) in zip(params, shapes) if g == 0],
+               "weight_decay": 0.1},
+              {"params": [p for p, (_, _, g) in zip(params, shapes) if g == 1],
+               "weight_decay": 0.0}]
+    opt = FusedAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+    st = opt._ensure_store()
+    opt._sync_state()
+    st.master.normal_(0, 0.02, generator=gen)
+    st.exp_avg.normal_(0, 1e-3, generator=gen)
+    st.exp_avg_sq.normal_(0, 1, generator=gen).abs_().mul_(1e-6)
+    st.steps.fill_(5.0)
+    with torch.no_grad():
+        for slot, p in enumerate(st.params):
+            p.copy_(st.views[slot]["master_param"])
+    grads = [torch.empty(s, dtype=torch.bfloat16, device=DEV) for _, s, _ in shapes]
+    for p, g in zip(params, grads):
+        g.copy_(torch.randn(g.shape, generator=gen, device=DEV) * 1e-3 * 2.0 ** 16)
+        p.grad = g
+    sc = GradScaler("cuda", init_scale=2.0 ** 16)
+    sc.scale(torch.ones((), device=DEV))
+
+    def checksum():
+        """Exact integer sums of every state word and every bf16 parameter."""
+        acc = [int(t.view(torch.int32).sum(dtype=torch.int64))
+               for t in (st.master, st.exp_avg, st.exp_avg_sq, st.steps)]
+        acc.append(sum(int(p.detach().view(torch.int16).sum(dtype=torch.int64))
+                       for p in params))
+        return acc
+
+    before = checksum()
+    grads[-1].view(-1)[17] = float("nan")
+    sc.unscale_(opt); clip_grad_norm_(params, 1.0); sc.step(opt); sc.update()
+    assert checksum() == before
+    assert float(sc.get_scale()) == 2.0 ** 15
+    grads[-1].view(-1)[17] = 0.0
+    # sample every tensor before the clean step
+    samp = {}
+    for slot, p in enumerate(st.params):
+        n = p.numel()
+        k = min(n, 4096)
+        ix = torch.randint(0, n, (k,), generator=gen, device=DEV)
+        v = st.views[slot]
+        samp[slot] = (ix, v["master_param"].view(-1)[ix].cpu().numpy(),
+                      v["exp_avg"].view(-1)[ix].cpu().numpy(),
+                      v["exp_avg_sq"].view(-1)[ix].cpu().numpy(),
+                      _bits(p.grad.view(-1)[ix]))
+    sc.unscale_(opt)
+    norm = clip_grad_norm_(params, 1.0)
+    sc.step(opt)
+    sc.update()
+    nrm = np.float32(norm.item())
+    assert abs(float(nrm) - _fp64_norm(grads, 2.0 ** -15)) <= 2 * np.spacing(nrm)
+    inv = O.inv_scale_of(2.0 ** 15)
+    coef = O.clip_coefficient(nrm, 1.0)
+    n_decay = len(groups[0]["params"])  # slots follow the groups: decay first
+    for slot, (ix, w, m, v, gb) in samp.items():
+        g = (O.unscale(O.bf16_bits_to_f32(gb), inv) * coef).astype(np.float32)
+        hp = O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.1 if slot < n_decay else 0.0)
+        w2, m2, v2 = O.adamw_update(w, m, v, g, hp, 6.0)
+        vv = st.views[slot]
+        np.testing.assert_array_equal(vv["master_param"].view(-1)[ix].cpu().numpy(), w2)
+        np.testing.assert_array_equal(vv["exp_avg"].view(-1)[ix].cpu().numpy(), m2)
+        np.testing.assert_array_equal(vv["exp_avg_sq"].view(-1)[ix].cpu().numpy(), v2)
