@@ -52,7 +52,6 @@ __device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
 // ---------------------------------------------------------------------------------------------
 
 struct GradBF16 {
-  using raw_t = uint16_t;
   struct vec_t { uint4 q; };
   static __device__ __forceinline__ vec_t load(const void* base, int64_t i) {
     return vec_t{ld_stream(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + i))};

@@ -39,7 +39,7 @@ import weakref
 from collections import defaultdict
 from dataclasses import dataclass
 from itertools import chain
-from typing import Any, Iterable
+from typing import Any
 
 import numpy as np
 import torch

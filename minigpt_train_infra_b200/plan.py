@@ -135,9 +135,6 @@ class ChunkPlan:
                                          device=device)
             _lib.call("b2o_workspace_init", self.workspace.data_ptr(), self.workspace.numel(),
                       torch.cuda.current_stream(device).cuda_stream)
-        # Per-slot exchange vector (n_slots + 1 doubles) inside the workspace.
-        exch_off = 64 + 8 * self.n_chunks
-        self.exch = self.workspace[exch_off:exch_off + 8 * (n_slots + 1)].view(torch.float64)
 
     def update_grads(self, grad_ptrs: np.ndarray) -> None:
         """Point the tensor entries at new gradient tensors (same sizes and dtypes, in entry

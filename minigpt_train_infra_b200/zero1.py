@@ -153,9 +153,6 @@ class CudaKernels:
                   None if norm is None else norm.data_ptr(), float(max_norm), peer_params,
                   n_ranks, my_rank, my_base, plan.workspace.data_ptr(), stream_ptr(plan.device))
 
-    def launches_per_step(self) -> int:
-        return 3  # stats, finalize, adamw
-
 
 class ZeroAdamW(torch.optim.Optimizer):
     """ZeRO-1 sharded :class:`FusedAdamW` (same constructor arguments plus the group)."""
@@ -246,7 +243,6 @@ class ZeroAdamW(torch.optim.Optimizer):
         self._plan = self._kernels.make_plan(self, self.geom.local_ranges())
         self._plans = [self._plan]
         self._pending: GradStats | None = None
-        self.last_allgather_report = None
         _REGISTRY.add(self)
 
     # ------------------------------------------------------------------------------------

@@ -133,3 +133,20 @@ def test_launching_entry_points_reject_bad_arguments_without_a_gpu():
                               0.0, None, None, None) == -1
     assert lib.b2o_finalize_norm(None, 1, 1, None, None, None) == -1
     assert lib.b2o_scaler_update(None, None, None, 2.0, 0.5, 2000, None) == -1
+    assert lib.b2o_adamw_step_dev(None, 0, None, 0, None, 1, 0, 0, None, None, None, None, 0.0,
+                                  None, None) == -1
+    peers = _lib.ptr_array([A, A])
+    t = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    ws = np.zeros(64, dtype=np.uint8)
+    # more ranks than one node holds, or a null peer, is rejected before any CUDA call
+    assert lib.b2o_reduce_scatter_stats(_lib.ptr_array([A] * 9), 9, A, 1.0, _lib.ptr(t), 1, None,
+                                        0, 1, None, _lib.ptr(ws), None, None) == -1
+    assert lib.b2o_reduce_scatter_stats(_lib.ptr_array([A, 0]), 2, A, 1.0, _lib.ptr(t), 1, None,
+                                        0, 1, None, _lib.ptr(ws), None, None) == -1
+    assert lib.b2o_adamw_step_bcast(_lib.ptr(t), 1, None, 0, _lib.ptr(g), 1, 0, None, None, None,
+                                    None, 0.0, peers, 2, 2, A, _lib.ptr(ws), None) == -1
+    for fn in ("b2o_peer_free", "b2o_peer_close"):
+        assert getattr(lib, fn)(None) == -1
+    assert lib.b2o_peer_alloc(0, None) == -1
+    assert lib.b2o_peer_export(None, None) == -1
+    assert lib.b2o_peer_import(None, None) == -1

@@ -88,6 +88,3 @@ class OracleKernels:
                 opt.flat_param[lo:hi] = torch.from_numpy(bits.copy()).view(torch.bfloat16)
         for slot, _, _ in plan.ranges:
             steps[slot] += 1.0
-
-    def launches_per_step(self) -> int:
-        return 0
