@@ -65,12 +65,37 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
   if (flags & B2O_STATS_CLEAR)
     for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
   __syncthreads();
-  for (int ti = warp; ti < n_tensors; ti += kWarps) {
-    const b2o_tensor& t = tensors[ti];
-    double sum = 0.0;
-    for (int k = lane; k < t.chunk_count; k += 32) sum += __ldcg(ws.chunk_sums + t.chunk_begin + k);
-    sum = warp_sum(sum);
-    if (lane == 0) exch[t.slot] = sum;
+  // One warp per tensor: warp w folds tensors w, w + kWarps, w + 2 kWarps, ...  The table
+  // entries of a warp's next 32 tensors are loaded at once (one per lane) and handed out by
+  // shuffles; each lane sums its chunk partials k, k+32, k+64, ... in that order, with eight
+  // loads in flight before the additions.
+  for (int base = 0; base < n_tensors; base += kWarps * 32) {
+    const int mine = base + lane * kWarps + warp;
+    int my_begin = 0, my_count = 0, my_slot = 0;
+    if (mine < n_tensors) {
+      my_begin = tensors[mine].chunk_begin;
+      my_count = tensors[mine].chunk_count;
+      my_slot = tensors[mine].slot;
+    }
+    const int batch = min(32, max(0, (n_tensors - base - warp + kWarps - 1) / kWarps));
+    for (int j = 0; j < batch; ++j) {
+      const int begin = __shfl_sync(0xffffffffu, my_begin, j);
+      const int count = __shfl_sync(0xffffffffu, my_count, j);
+      const int slot = __shfl_sync(0xffffffffu, my_slot, j);
+      const double* part = ws.chunk_sums + begin;
+      double sum = 0.0;
+      int k = lane;
+      for (; k + 7 * 32 < count; k += 8 * 32) {
+        double a[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = __ldcg(part + k + u * 32);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sum += a[u];
+      }
+      for (; k < count; k += 32) sum += __ldcg(part + k);
+      sum = warp_sum(sum);
+      if (lane == 0) exch[slot] = sum;
+    }
   }
   if (threadIdx.x == 0) {
     const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
@@ -106,14 +131,13 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
   bool bad = false;
 
 #if B2O_STATS_SCHED == 1
-  // dynamic: thread 0 takes the next chunk from a global counter one chunk ahead, so the
-  // chunks being read stay a compact window of the gradient buffer
+  // dynamic: thread 0 takes the next chunk from a global counter, so the chunks being read stay
+  // a compact window of the gradient buffer
   __shared__ unsigned int s_tile[2];
   if (threadIdx.x == 0) s_tile[0] = atomicAdd(ws.stats_tile, 1u);
   __syncthreads();
   int buf = 0;
   for (int64_t c = s_tile[0]; c < n_chunks;) {
-    if (threadIdx.x == 0) s_tile[buf ^ 1] = atomicAdd(ws.stats_tile, 1u);
 #else
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
 #endif
@@ -157,6 +181,12 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
       const double u = (double)__fmul_rn(G::load1(g, ch.begin + i, bad), inv);
       acc += u * u;  // exact: a squared fp32 value fits in fp64
     }
+#if B2O_STATS_SCHED == 1
+    // The next chunk is claimed only once this one is read (the claim's latency overlaps the
+    // block sum), so a CTA that started early cannot hold a second chunk while another CTA has
+    // none; a chunk is many loop iterations long here.
+    if (threadIdx.x == 0) s_tile[buf ^ 1] = atomicAdd(ws.stats_tile, 1u);
+#endif
     const double total = block_sum(acc, scratch);
     if (threadIdx.x == 0) ws.chunk_sums[c] = total;
 #if B2O_STATS_SCHED == 1

@@ -112,3 +112,51 @@ def test_training_loop_tracks_torch_reference():
     assert n_plans == 1  # autograd's reallocated gradients only patch the pointers
     steps = {float(s["step"]) for s in opt.state.values()}
     assert steps == {40.0}
+
+
+def test_fp16_autocast_loop_follows_the_scaler_contract():
+    """The reference's own mixed-precision mode (``train.py:366-370,479-491``; GradScaler enabled
+    for fp16 autocast): fp32 parameters, fp16 activations, scaled fp32 gradients.  A large initial
+    scale forces overflow skips and a short growth interval forces growth; every step's skip
+    decision must equal the gradients' own finiteness, a skipped step must leave parameters and
+    step counters untouched, and the scale must follow backoff/growth exactly."""
+    from minigpt_train_infra_b200 import (FusedAdamW, GradScaler, build_adamw_param_groups,
+                                          clip_grad_norm_)
+    torch.manual_seed(0)
+    model = TinyDecoder().to(DEV)
+    opt = FusedAdamW(build_adamw_param_groups(model, 0.1), lr=3e-3, betas=(0.9, 0.95), eps=1e-8)
+    scaler = GradScaler("cuda", init_scale=2.0 ** 24, growth_interval=4)
+    gen = torch.Generator(device=DEV).manual_seed(1)
+    scale, tracker, skips, growths, losses = 2.0 ** 24, 0, 0, 0, []
+    params = list(model.parameters())
+    for step in range(40):
+        for g in opt.param_groups:
+            g["lr"] = _cosine(step)
+        opt.zero_grad(set_to_none=True)
+        x = torch.randint(0, 97, (16, 32), generator=gen, device=DEV)
+        with torch.autocast("cuda", dtype=torch.float16):
+            logits = model(x)
+        loss = F.cross_entropy(logits.float().view(-1, 97), ((x * 3 + 1) % 97).view(-1))
+        scaler.scale(loss).backward()
+        bad = not all(bool(torch.isfinite(p.grad).all()) for p in params)
+        before = [p.detach().clone() for p in params]
+        scaler.unscale_(opt)
+        clip_grad_norm_(params, 1.0)
+        scaler.step(opt)
+        scaler.update()
+        if bad:
+            skips += 1
+            scale, tracker = scale * 0.5, 0
+            assert all(torch.equal(a, p) for a, p in zip(before, params))
+        else:
+            losses.append(float(loss.detach()))
+            tracker += 1
+            if tracker == 4:
+                scale, tracker, growths = scale * 2.0, 0, growths + 1
+            assert not any(torch.equal(a, p) for a, p in zip(before, params[:1]))
+        assert scaler.get_scale() == scale
+        assert int(scaler._growth_tracker) == tracker
+        assert {float(s["step"]) for s in opt.state.values()} <= {float(step + 1 - skips)}
+    assert skips >= 1 and growths >= 1
+    assert {float(s["step"]) for s in opt.state.values()} == {40.0 - skips}
+    assert losses[-1] < 0.6 * losses[0], "the fp16-autocast model must learn the task"
