@@ -669,6 +669,14 @@ def run_dp_step(args) -> None:
     step_ms = timed(one_step, args.steps)
     copy_ms = timed(lambda: opt.flat_grad.copy_(local_grads), args.steps)
     ms = step_ms - copy_ms
+    # Every rank must receive the other ranks' gradients for its shard (reduce-scatter) and the
+    # other ranks' updated bf16 shards (gather): 2 x 2 bytes x P x (N-1)/N over NVLink, whoever
+    # moves them; at the measured 770 GB/s per direction that bounds the step from below.
+    recv = 4 * P * (ws - 1) / ws
+    nvlink = {"bound": "nvlink", "recv_bytes_per_rank": int(recv),
+              "achieved": round(recv / (ms / 1e3) / 1e9, 1), "peak": 770.0, "unit": "GB/s",
+              "frac": round(recv / (ms / 1e3) / 1e9 / 770.0, 4),
+              "peak_kind": "measured peer copy bandwidth per direction"}
     if rank == 0:
         emit_result({
             "metric": "ZeRO-1 data-parallel step incl. grad reduce-scatter and param gather",
@@ -682,7 +690,8 @@ def run_dp_step(args) -> None:
                        "NCCL reduce_scatter_tensor + all_gather_into_tensor around the kernels",
                        "note": "the timed loop copies fresh local grads each step (a stand-in "
                                "for backward); that copy is timed separately and subtracted",
-                       "grad_copy_ms": round(copy_ms, 4)}})
+                       "grad_copy_ms": round(copy_ms, 4)},
+            "roofline": nvlink})
     opt.close()
     dist.barrier()
     dist.destroy_process_group()
