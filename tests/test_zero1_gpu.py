@@ -1,5 +1,5 @@
-"""ZeroAdamW on GPUs: one rank must reproduce FusedAdamW bit for bit; two NCCL ranks (when two
-GPUs are visible) must reproduce the one-GPU result."""
+"""ZeroAdamW on GPUs: one rank must reproduce FusedAdamW bit for bit; 2, 4 or 8 NCCL ranks (as
+many as the box has GPUs) must reproduce the one-GPU result."""
 
 from __future__ import annotations
 
@@ -14,6 +14,9 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(300, 129), (129,), (5,), (1024, 64), (3, 3, 3), (70001,), (0,), (4096, 33)]
+# world sizes to run: every one of 2, 4, 8 that the visible GPUs allow (2 -> skipped on one GPU)
+WORLDS = [w for w in (2, 4, 8) if w <= torch.cuda.device_count()] or [2]
+needs_world = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 
 
 def _init(device, dtype=torch.bfloat16):
@@ -96,11 +99,12 @@ def _nccl_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_zero_two_nccl_ranks_match_one_gpu(tmp_path):
+@needs_world
+@pytest.mark.parametrize("world", WORLDS)
+def test_zero_nccl_ranks_match_one_gpu(tmp_path, world):
     from minigpt_train_infra_b200 import GradScaler, ZeroAdamW
-    port = 29500 + os.getpid() % 1000
-    mp.start_processes(_nccl_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+    port = 29500 + os.getpid() % 1000 + world
+    mp.start_processes(_nccl_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     device = torch.device("cuda", 0)
     _, params, groups = _init(device)
@@ -109,7 +113,7 @@ def test_zero_two_nccl_ranks_match_one_gpu(tmp_path):
     sc.scale(torch.ones((), device=device))
     norms = _run(opt, params, sc, device, torch.bfloat16, copy_grads=True)
     flat1 = opt.flat_param.float().cpu().numpy()
-    for r in range(2):
+    for r in range(world):
         z = np.load(tmp_path / f"nccl{r}.npz")
         assert float(z["scale"]) == float(sc.get_scale())
         np.testing.assert_array_equal(z["steps"], opt.steps.cpu().numpy())
@@ -132,7 +136,8 @@ def _local_grads(step, rank, device):
 
 
 def _reduced_grads(step, world, device):
-    """bf16(0.5 * (g_0 + g_1 + ...)) summed in fp32 in rank order: the fused kernel's rule."""
+    """bf16((g_0 + g_1 + ...) * (1/world)) summed in fp32 in rank order: the fused kernel's
+    rule."""
     per_rank = [_local_grads(step, r, "cpu") for r in range(world)]
     out = []
     for t in range(len(SHAPES)):
@@ -179,15 +184,16 @@ def _dp_worker(rank, world, port, out_dir, peer_memory):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@needs_world
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("peer_memory", [True, False])
-def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_memory):
-    """Two ranks with different local gradients: the fused peer-memory reduce-scatter (or NCCL's)
+def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_memory, world):
+    """Ranks with different local gradients: the fused peer-memory reduce-scatter (or NCCL's)
     plus the step must equal one GPU stepping on the averaged gradients; with peer memory the
     updated parameters reach every rank through the fused broadcast."""
     from minigpt_train_infra_b200 import GradScaler, FusedAdamW, clip_grad_norm_
-    port = 29700 + os.getpid() % 1000 + (0 if peer_memory else 1)
-    mp.start_processes(_dp_worker, args=(2, port, str(tmp_path), peer_memory), nprocs=2,
+    port = 29700 + os.getpid() % 1000 + 16 * world + (0 if peer_memory else 1)
+    mp.start_processes(_dp_worker, args=(world, port, str(tmp_path), peer_memory), nprocs=world,
                        join=True, start_method="spawn")
     device = torch.device("cuda", 0)
     _, params, groups = _init(device)
@@ -196,7 +202,7 @@ def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_mem
     sc.scale(torch.ones((), device=device))
     norms = []
     for s in range(5):
-        for p, g in zip(params, _reduced_grads(s, 2, device)):
+        for p, g in zip(params, _reduced_grads(s, world, device)):
             p.grad = g
         sc.unscale_(opt)
         norms.append(float(clip_grad_norm_(params, 1.0)))
@@ -204,18 +210,29 @@ def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_mem
         sc.update()
     # the flat buffer holds the tensors in param-group order (decay group first)
     ref_flat = [p.detach().float().cpu().numpy().ravel() for g in groups for p in g["params"]]
-    for r in range(2):
+    for r in range(world):
         z = np.load(tmp_path / f"dp{r}.npz")
         assert float(z["scale"]) == float(sc.get_scale())
+        # NCCL sums more than two bf16 addends with a bf16 rounding per partial sum, so its
+        # reduced gradients (and the norm) differ from the fp32 rule by bf16 roundings
+        loose = not peer_memory and world > 2
         for a, b in zip(z["norms"], norms):
-            assert (np.isnan(a) and np.isnan(b)) or abs(a - b) <= 2 * np.spacing(np.float32(b))
+            tol = 1e-4 * abs(b) if loose else 2 * np.spacing(np.float32(b))
+            assert (np.isnan(a) and np.isnan(b)) or abs(a - b) <= tol
         off = 0
         for t, w in enumerate(ref_flat):
             n = w.size
             got = z["flat"][off:off + n]
             if peer_memory:
                 np.testing.assert_array_equal(got, w)
-            elif n:
-                # NCCL reduces bf16 in its own order; equal up to bf16 rounding of the sums
+            elif n and not loose:
+                # two bf16 addends: NCCL's sum is their exact sum rounded once, as in the rule
                 assert np.max(np.abs(got - w)) <= 2 ** -7 * np.max(np.abs(w)) + 1e-12
+            elif n:
+                # a gradient sum near zero can change sign under NCCL's roundings; four applied
+                # steps (one skipped) move an element by at most about 1.5 lr each, and almost
+                # every element must agree to bf16 rounding
+                d = np.abs(got - w)
+                assert np.max(d) <= 2 * 4 * 1.5e-3 + 1e-3
+                assert np.mean(d <= 2 ** -7 * np.max(np.abs(w)) + 1e-12) >= 0.98
             off += (n + 63) // 64 * 64
