@@ -65,10 +65,11 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
   if (flags & B2O_STATS_CLEAR)
     for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
   __syncthreads();
-  // One warp per tensor: warp w folds tensors w, w + kWarps, w + 2 kWarps, ...  The table
-  // entries of a warp's next 32 tensors are loaded at once (one per lane) and handed out by
-  // shuffles; each lane sums its chunk partials k, k+32, k+64, ... in that order, with eight
-  // loads in flight before the additions.
+  // Every thread loads the table entry of one tensor (warp w, lane l: tensor w + kWarps * l of
+  // each block of kWarps * 32).  A tensor of at most one chunk is finished by that thread: its
+  // sum is its one partial (or 0).  Longer tensors are folded by their warp, one at a time: each
+  // lane sums the chunk partials k, k+32, k+64, ... in that order, with eight loads in flight
+  // before the additions, then the warp's xor tree adds the 32 lane sums.
   for (int base = 0; base < n_tensors; base += kWarps * 32) {
     const int mine = base + lane * kWarps + warp;
     int my_begin = 0, my_count = 0, my_slot = 0;
@@ -76,9 +77,12 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
       my_begin = tensors[mine].chunk_begin;
       my_count = tensors[mine].chunk_count;
       my_slot = tensors[mine].slot;
+      if (my_count <= 1) exch[my_slot] = my_count ? __ldcg(ws.chunk_sums + my_begin) : 0.0;
     }
-    const int batch = min(32, max(0, (n_tensors - base - warp + kWarps - 1) / kWarps));
-    for (int j = 0; j < batch; ++j) {
+    unsigned int multi = __ballot_sync(0xffffffffu, mine < n_tensors && my_count > 1);
+    while (multi) {
+      const int j = __ffs(multi) - 1;
+      multi &= multi - 1;
       const int begin = __shfl_sync(0xffffffffu, my_begin, j);
       const int count = __shfl_sync(0xffffffffu, my_count, j);
       const int slot = __shfl_sync(0xffffffffu, my_slot, j);
