@@ -34,6 +34,7 @@ sys.path.insert(0, str(ROOT))
 from minigpt_train_infra_b200 import workloads  # noqa: E402
 
 METRIC = "fused AdamW step Gparams/s and HBM GB/s vs peak at 1/2/4/8 B200"
+L2_BYTES = 126 * 2 ** 20
 ADAMW_BYTES = 28   # read g(2)+w,m,v(12); write w,m,v(12)+bf16 param(2)
 STATS_BYTES = 2    # read g
 FALLBACK_HBM_GBS = 6650.0
@@ -316,6 +317,18 @@ def run_ours(args) -> None:
     for _ in range(args.warmup):
         one_step()
     torch.cuda.synchronize()
+    # Workloads whose per-step footprint (bf16 grad + bf16 param + fp32 master/m/v = 16 B per
+    # owned parameter) is under 4x the 126 MB L2 get L2 flushed before every timed step (a
+    # 256 MB write outside the step's events); larger ones stream far more than L2 holds.
+    P_own = opt.local_numel() if ws > 1 else P
+    footprint = 16 * P_own
+    flush_buf = torch.empty(64 << 20, dtype=torch.float32, device=device) \
+        if footprint < 4 * L2_BYTES else None
+
+    def flush_l2():
+        if flush_buf is not None:
+            flush_buf.zero_()
+
     eager_phases = None
     if args.graph and ws == 1:
         # a replay cannot be split into its kernels with events, so the per-kernel times (and the
@@ -323,6 +336,7 @@ def run_ours(args) -> None:
         k = max(3, min(args.steps, 10))
         pev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(k)]
         for e in pev:
+            flush_l2()
             one_step(e)
         torch.cuda.synchronize()
         eager_phases = [statistics.mean(e[i].elapsed_time(e[i + 1]) for e in pev)
@@ -354,9 +368,13 @@ def run_ours(args) -> None:
             torch.distributed.barrier()
             torch.cuda.synchronize()
         for i in range(args.steps):
+            flush_l2()
             one_step(evs[i])
         torch.cuda.synchronize()
-    total_ms = evs[0][0].elapsed_time(evs[-1][3])
+    if flush_buf is None:
+        total_ms = evs[0][0].elapsed_time(evs[-1][3])
+    else:  # the flushes between steps are not step time
+        total_ms = sum(e[0].elapsed_time(e[3]) for e in evs)
     stats_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     adamw_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     upd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
@@ -406,8 +424,12 @@ def run_ours(args) -> None:
                            "stores)" if args.peer_memory else
                            " (sharded update; bf16 all-gather reported under allgather)")
                           if ws > 1 else ""),
-                "l2": "no flush: every step streams the whole optimizer state "
-                      f"({16 * P_local / 1e9:.1f} GB per rank), far above the 126 MB L2",
+                "l2": (f"flushed before every timed step (256 MB write outside the step's "
+                       f"events): the step's {footprint / 1e6:.0f} MB footprint is under 4x the "
+                       "126 MB L2") if flush_buf is not None else
+                      ("no flush: every step streams the whole optimizer state "
+                       f"({footprint / 1e9:.1f} GB per rank, {footprint / L2_BYTES:.0f}x the "
+                       "126 MB L2)"),
                 "hp": {"lr": LR, "betas": BETAS, "eps": EPS, "weight_decay": WD, "clip": CLIP,
                        "loss_scale": scale},
             },
