@@ -148,6 +148,9 @@ def _reduced_grads(step, world, device):
     return out
 
 
+GAP_SENTINEL = 0x7FC1  # a bf16 NaN
+
+
 def _dp_worker(rank, world, port, out_dir, peer_memory):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -164,6 +167,17 @@ def _dp_worker(rank, world, port, out_dir, peer_memory):
         _, params, groups = _init(device)
         opt = ZeroAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, peer_memory=peer_memory,
                         reduce_grads=True)
+        # guard bands: the alignment gaps and the tail padding of both flat buffers hold a bf16
+        # NaN; with peer memory no kernel may read them (the NaN would raise the inf flag) or
+        # write them (they are compared afterwards), on this rank or through a peer mapping
+        covered = torch.zeros(opt.geom.padded, dtype=torch.bool)
+        for p, off in zip(opt.params, opt.geom.offsets):
+            covered[off:off + p.numel()] = True
+        gaps = (~covered).nonzero().squeeze(1).to(device)
+        if peer_memory:
+            opt.flat_grad.view(torch.int16)[gaps] = GAP_SENTINEL
+            opt.flat_param.view(torch.int16)[gaps] = GAP_SENTINEL
+            dist.barrier()
         sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
         sc.scale(torch.ones((), device=device))
         norms = []
@@ -177,7 +191,9 @@ def _dp_worker(rank, world, port, out_dir, peer_memory):
         torch.cuda.synchronize()
         np.savez(os.path.join(out_dir, f"dp{rank}.npz"), norms=np.array(norms),
                  scale=float(sc.get_scale()), flat=opt.flat_param.float().cpu().numpy(),
-                 steps=opt.steps.cpu().numpy())
+                 steps=opt.steps.cpu().numpy(), n_gaps=gaps.numel(),
+                 grad_gaps=opt.flat_grad.view(torch.int16)[gaps].cpu().numpy(),
+                 param_gaps=opt.flat_param.view(torch.int16)[gaps].cpu().numpy())
         opt.close()
         dist.barrier()
     finally:
@@ -213,6 +229,10 @@ def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_mem
     for r in range(world):
         z = np.load(tmp_path / f"dp{r}.npz")
         assert float(z["scale"]) == float(sc.get_scale())
+        if peer_memory:
+            assert int(z["n_gaps"]) > 0
+            assert (z["grad_gaps"] == GAP_SENTINEL).all(), "a gradient gap was written"
+            assert (z["param_gaps"] == GAP_SENTINEL).all(), "a parameter gap was written"
         # NCCL sums more than two bf16 addends with a bf16 rounding per partial sum, so its
         # reduced gradients (and the norm) differ from the fp32 rule by bf16 roundings
         loose = not peer_memory and world > 2
