@@ -751,7 +751,8 @@ def run_reference(args) -> None:
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
         "config": {"workload": f"{name}: bounded sample (see cpu_baseline.sample)",
                    "parallelism": "host CPU, rank 0 only"},
-        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline": {**{k: cpu[k] for k in ("unit", "cores", "kind", "sample")},
+                         "value": round(cpu["value"], 4)},
         "e2e": {"value": round(cpu["value"], 4), "unit": "Gparams/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
