@@ -78,6 +78,8 @@ class PeerBuffer:
 
     @property
     def ptr_array(self):
+        if self._ptr_array is None:
+            raise RuntimeError("peer buffer is closed: its peer mappings were released")
         return self._ptr_array
 
     def close(self) -> None:
@@ -85,6 +87,7 @@ class PeerBuffer:
         Call on every rank, with every kernel that touches peer memory finished, then
         synchronise the ranks before any of them frees its buffer."""
         lib = _lib.load()
+        self._ptr_array = None  # no kernel may be handed the released mappings
         for p in self._imports:
             lib.b2o_peer_close(p)
         self._imports = []

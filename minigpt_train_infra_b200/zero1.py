@@ -279,7 +279,8 @@ class ZeroAdamW(torch.optim.Optimizer):
         dist.all_reduce(self._bar, group=self.pg)
 
     def close(self) -> None:
-        """Release the peer mappings (with ``peer_memory``); call on every rank."""
+        """Release the peer mappings (with ``peer_memory``); call on every rank.  A step after
+        this raises instead of launching kernels on the released mappings."""
         if self._peer_bufs:
             torch.cuda.synchronize(self.device)
             dist.barrier(group=self.pg)
@@ -474,8 +475,9 @@ class ZeroAdamW(torch.optim.Optimizer):
         if self.reduce_grads and self.world_size > 1:
             if self.peer_memory:
                 gb = self._peer_bufs[1]
+                peers = gb.ptr_array  # raises after close(), before any collective is issued
                 self._barrier()  # every rank's gradients are complete
-                self._kernels.reduce_scatter_stats(self._plan, gb.ptr_array, self.world_size,
+                self._kernels.reduce_scatter_stats(self._plan, peers, self.world_size,
                                                    gb.local.data_ptr(), self.grad_scale_factor,
                                                    loss_scale, self.exch_local)
             else:

@@ -195,6 +195,14 @@ def _dp_worker(rank, world, port, out_dir, peer_memory):
                  grad_gaps=opt.flat_grad.view(torch.int16)[gaps].cpu().numpy(),
                  param_gaps=opt.flat_param.view(torch.int16)[gaps].cpu().numpy())
         opt.close()
+        if peer_memory:
+            # every rank raises at the same point, before any collective of the step
+            try:
+                sc.unscale_(opt)
+            except RuntimeError as e:
+                assert "closed" in str(e)
+            else:
+                raise AssertionError("a step after close() must raise")
         dist.barrier()
     finally:
         dist.destroy_process_group()
