@@ -119,7 +119,9 @@ def test_fp16_autocast_loop_follows_the_scaler_contract():
     for fp16 autocast): fp32 parameters, fp16 activations, scaled fp32 gradients.  A large initial
     scale forces overflow skips and a short growth interval forces growth; every step's skip
     decision must equal the gradients' own finiteness, a skipped step must leave parameters and
-    step counters untouched, and the scale must follow backoff/growth exactly."""
+    step counters untouched, and the scale must follow backoff/growth exactly.  As in the
+    reference loop, each step accumulates two micro-batches (``loss / 2``) and keeps a running
+    maximum of the returned norm tensor."""
     from minigpt_train_infra_b200 import (FusedAdamW, GradScaler, build_adamw_param_groups,
                                           clip_grad_norm_)
     torch.manual_seed(0)
@@ -133,15 +135,18 @@ def test_fp16_autocast_loop_follows_the_scaler_contract():
         for g in opt.param_groups:
             g["lr"] = _cosine(step)
         opt.zero_grad(set_to_none=True)
-        x = torch.randint(0, 97, (16, 32), generator=gen, device=DEV)
-        with torch.autocast("cuda", dtype=torch.float16):
-            logits = model(x)
-        loss = F.cross_entropy(logits.float().view(-1, 97), ((x * 3 + 1) % 97).view(-1))
-        scaler.scale(loss).backward()
+        for _micro in range(2):  # gradient accumulation (train.py's micro-step loop)
+            x = torch.randint(0, 97, (16, 32), generator=gen, device=DEV)
+            with torch.autocast("cuda", dtype=torch.float16):
+                logits = model(x)
+                loss = F.cross_entropy(logits.float().view(-1, 97), ((x * 3 + 1) % 97).view(-1))
+            scaler.scale(loss / 2).backward()
         bad = not all(bool(torch.isfinite(p.grad).all()) for p in params)
         before = [p.detach().clone() for p in params]
         scaler.unscale_(opt)
-        clip_grad_norm_(params, 1.0)
+        norm = clip_grad_norm_(params, 1.0)
+        norm_max = norm.detach().float() if step == 0 else torch.maximum(
+            norm_max, norm.detach().float())
         scaler.step(opt)
         scaler.update()
         if bad:
@@ -158,5 +163,6 @@ def test_fp16_autocast_loop_follows_the_scaler_contract():
         assert int(scaler._growth_tracker) == tracker
         assert {float(s["step"]) for s in opt.state.values()} <= {float(step + 1 - skips)}
     assert skips >= 1 and growths >= 1
+    assert not bool(torch.isfinite(norm_max))  # an overflowing step's norm is inf or NaN
     assert {float(s["step"]) for s in opt.state.values()} == {40.0 - skips}
     assert losses[-1] < 0.6 * losses[0], "the fp16-autocast model must learn the task"
