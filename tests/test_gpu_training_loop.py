@@ -166,3 +166,63 @@ def test_fp16_autocast_loop_follows_the_scaler_contract():
     assert not bool(torch.isfinite(norm_max))  # an overflowing step's norm is inf or NaN
     assert {float(s["step"]) for s in opt.state.values()} == {40.0 - skips}
     assert losses[-1] < 0.6 * losses[0], "the fp16-autocast model must learn the task"
+
+
+def test_tiny_gpu_config_bf16_autocast_tracks_torch():
+    """The reference's ``configs/tiny_gpu.json`` recipe: 4 layers, 4 heads, 128 wide, block 128,
+    batch 16, 4 accumulation micro-steps, bf16 autocast over fp32 parameters with the scaler
+    disabled (GradScaler is enabled for fp16 only, ``train.py:366-370``), lr 6e-4 with 20 warm-up
+    steps, weight decay 0.01 on matrices, betas (0.9, 0.95), clip 1.0.  Against torch's own
+    ``AdamW(fused=True)`` + ``GradScaler(enabled=False)`` + ``clip_grad_norm_`` from the same
+    initial weights and batches: after the first step the weights agree to the rounding of the
+    two update implementations; over 30 steps the losses and norms track to 2e-3 and the
+    weights on average to 1e-5 (an element whose gradient is near zero may take Adam's full
+    +-lr step one way in one run and the other way in the other)."""
+    from minigpt_train_infra_b200 import (FusedAdamW, GradScaler, build_adamw_param_groups,
+                                          clip_grad_norm_)
+
+    def run(fused):
+        torch.manual_seed(1337)
+        model = TinyDecoder(vocab=65, d=128, n_layer=4, n_head=4, block=128).to(DEV)
+        groups = build_adamw_param_groups(model, 0.01)
+        if fused:
+            opt = FusedAdamW(groups, lr=6e-4, betas=(0.9, 0.95), eps=1e-8)
+            scaler, clip = GradScaler("cuda", enabled=False), clip_grad_norm_
+        else:
+            opt = torch.optim.AdamW(groups, lr=6e-4, betas=(0.9, 0.95), eps=1e-8, fused=True)
+            scaler = torch.amp.GradScaler("cuda", enabled=False)
+            clip = torch.nn.utils.clip_grad_norm_
+        gen = torch.Generator(device=DEV).manual_seed(7)
+        losses, norms = [], []
+        for step in range(30):
+            for g in opt.param_groups:
+                g["lr"] = _cosine(step, base=6e-4, warm=20, total=200, low=6e-5)
+            opt.zero_grad(set_to_none=True)
+            for _micro in range(4):
+                x = torch.randint(0, 65, (16, 128), generator=gen, device=DEV)
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    logits = model(x)
+                    loss = F.cross_entropy(logits.float().view(-1, 65), ((x * 3 + 1) % 65).view(-1))
+                scaler.scale(loss / 4).backward()
+            scaler.unscale_(opt)
+            norms.append(float(clip(model.parameters(), 1.0)))
+            scaler.step(opt)
+            scaler.update()
+            losses.append(float(loss.detach()))
+            if step == 0:
+                first = [p.detach().clone() for p in model.parameters()]
+        return losses, norms, [p.detach().clone() for p in model.parameters()], opt, first
+
+    ours, our_norms, our_w, opt, our_first = run(True)
+    ref, ref_norms, ref_w, _, ref_first = run(False)
+    for a, b in zip(our_first, ref_first):
+        assert float((a - b).abs().max()) <= 1e-6
+    assert ours[-1] < ours[0], "the loss must fall"
+    for a, b in zip(ours, ref):
+        assert abs(a - b) <= 2e-3 * abs(b)
+    for a, b in zip(our_norms, ref_norms):
+        assert abs(a - b) <= 2e-3 * abs(b)
+    diffs = torch.cat([(a - b).abs().flatten() for a, b in zip(our_w, ref_w)])
+    assert float(diffs.mean()) <= 1e-5
+    assert float(diffs.max()) <= 2e-2
+    assert {float(s["step"]) for s in opt.state.values()} == {30.0}
