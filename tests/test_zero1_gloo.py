@@ -102,7 +102,7 @@ def _worker_equivalence(rank, world, init_file, out_dir, dtype_name):
         scaler.scale(torch.ones(()))
         order = [p for g in groups for p in g["params"]]
         idx = [next(i for i, q in enumerate(params) if q is p) for p in order]
-        # an inf at step 2 in the last tensor: owned by the last rank only
+        # an inf at step 2 in the last tensor, inside the last rank's shard
         found, norms, scales = [], [], []
         for step in range(5):
             inf_at = (len(SHAPES) - 1, 2040) if step == 2 else None
@@ -154,9 +154,8 @@ def _single_process_oracle(dtype):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("dtype_name", ["bfloat16", "float32"])
-def test_zero1_two_ranks_match_single_process_oracle(tmp_path, dtype_name):
-    world = 2
+@pytest.mark.parametrize("dtype_name,world", [("bfloat16", 2), ("float32", 2), ("bfloat16", 3)])
+def test_zero1_ranks_match_single_process_oracle(tmp_path, dtype_name, world):
     init_file = tmp_path / "rdzv"
     mp.spawn(_worker_equivalence, args=(world, str(init_file), str(tmp_path), dtype_name),
              nprocs=world, join=True)
