@@ -10,7 +10,8 @@
 //   element -> fp32 sum of squares over one 8-element vector (fma chain)
 //   vector  -> fp64 per-thread sum -> fixed-order CTA sum = one fp64 partial per chunk
 //   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order with a
-//              fixed lane-strided walk + xor-shuffle tree into exch[slot]
+//              fixed lane-strided walk + xor-shuffle tree into exch[slot] (a tensor of one
+//              chunk: its partial, copied by one thread -- the same value the walk gives)
 //   slot    -> per-tensor norm fp32(sqrt(sum)), total fp32(sqrt(sum of squared norms)); the
 //              same two-level structure as clip_grad.py:_get_total_norm.
 #include <cuda_runtime.h>
