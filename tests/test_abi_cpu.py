@@ -150,3 +150,44 @@ def test_launching_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.b2o_peer_alloc(0, None) == -1
     assert lib.b2o_peer_export(None, None) == -1
     assert lib.b2o_peer_import(None, None) == -1
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_planner_random_tables(seed):
+    """Random tables: every element of every tensor is in exactly one chunk of its own tensor,
+    chunks are contiguous per tensor and in table order, no chunk is longer than chunk_elems,
+    and the vector flag is set exactly when every non-null pointer is 16-byte aligned."""
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(1, 40))
+    chunk = int(8 * rng.integers(1, 64))
+    rows, aligned = [], []
+    for i in range(n):
+        numel = int(rng.choice([0, 1, 7, 8, 9, int(rng.integers(1, 5000))]))
+        offs = [int(rng.choice([0, 0, 0, 2, 4, 8])) for _ in range(5)]
+        fp32_param = bool(rng.integers(0, 2))
+        ptrs = [A + 0x100000 * (i + 1) + o for o in offs]
+        if fp32_param:
+            ptrs[1] = 0
+        rows.append((*ptrs, numel, int(rng.integers(0, 3)), i, 0, 0, 0, 0))
+        aligned.append(all(p % 16 == 0 for p in ptrs if p))
+    t = _table(rows)
+    perm = rng.permutation(n)  # slots need not follow table order
+    t["slot"] = perm
+    st, c = _plan(t, chunk_elems=chunk, n_groups=3, n_slots=n)
+    assert st == 0
+    pos = 0
+    for i in range(n):
+        cnt = int(t["chunk_count"][i])
+        assert int(t["chunk_begin"][i]) == pos
+        mine = c[pos:pos + cnt]
+        assert (mine["tensor"] == i).all()
+        if cnt:
+            assert mine["begin"][0] == 0 and mine["end"][-1] == rows[i][5]
+            assert (mine["end"][:-1] == mine["begin"][1:]).all()
+            assert ((mine["end"] - mine["begin"]) <= chunk).all()
+            assert ((mine["end"] - mine["begin"]) > 0).all()
+        else:
+            assert rows[i][5] == 0
+        assert bool(t["flags"][i] & _lib.FLAG_VECTOR) == aligned[i]
+        pos += cnt
+    assert pos == len(c)
