@@ -111,3 +111,38 @@ def test_sweep_covers_the_cases():
     assert {c["bf16"] for c in cfgs} == {True, False}
     assert sum(len(c[2]) == 2 for c in cases) >= 3                          # two param groups
     assert {c["growth_interval"] for c in cfgs} >= {1, 2}                   # growth happens
+
+
+@pytest.mark.parametrize("start_step", [999.0, 123456.0])
+def test_oracle_matches_torch_chain_from_a_late_step(start_step):
+    """Bias corrections far from step 1 (BASELINE config 2 stores step 999): the state is loaded
+    into torch's AdamW at ``start_step`` with non-zero moments, then two steps run on both."""
+    shapes = [(257,), (64, 33), (5,)]
+    gen = torch.Generator().manual_seed(99)
+    w0 = [torch.randn(s, generator=gen) * 0.02 for s in shapes]
+    m0 = [torch.randn(s, generator=gen) * 1e-3 for s in shapes]
+    v0 = [torch.randn(s, generator=gen).abs() * 1e-6 for s in shapes]
+    chain = ReferenceChain([w0], [0.1], ChainConfig(lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
+                                                    max_norm=1.0, scaler_enabled=True,
+                                                    init_scale=2.0 ** 16))
+    sd = chain.opt.state_dict()
+    sd["state"] = {i: {"step": torch.tensor(start_step), "exp_avg": m0[i].clone(),
+                       "exp_avg_sq": v0[i].clone()} for i in range(len(shapes))}
+    chain.opt.load_state_dict(sd)
+    states = [O.TensorState(w=w0[i].numpy().copy(), m=m0[i].numpy().copy(),
+                            v=v0[i].numpy().copy(), step=start_step) for i in range(len(shapes))]
+    scaler = O.ScalerState(scale=np.float32(2.0 ** 16))
+    hp = [O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.1)]
+    for step in range(2):
+        g = torch.Generator().manual_seed(500 + step)
+        gs = [(torch.randn(s, generator=g) * 1e-2 * 2.0 ** 16).to(torch.bfloat16).float()
+              for s in shapes]
+        ref = chain.step(gs)
+        O.optimizer_step(states, [x.numpy() for x in gs], hp, scaler, 1.0,
+                         norm=np.float32(ref["norm"]))
+        for st, p in zip(states, chain.params):
+            s = chain.state_of(p)
+            assert st.step == float(s["step"]) == start_step + step + 1
+            np.testing.assert_array_equal(st.m, s["exp_avg"].numpy())
+            np.testing.assert_array_equal(st.v, s["exp_avg_sq"].numpy())
+            assert _normwise(st.w, p.detach().numpy()) <= 1e-6
