@@ -225,7 +225,8 @@ def scaler_update(scale: np.float32, tracker: int, found_inf: bool, growth_facto
         return F32(F64(scale) * backoff_factor), 0
     successful = tracker + 1
     if successful == growth_interval:
-        grown = F32(F64(scale) * growth_factor)
+        with np.errstate(over="ignore"):  # a product past fp32's range rounds to inf: not kept
+            grown = F32(F64(scale) * growth_factor)
         return (grown if np.isfinite(grown) else scale), 0
     return scale, successful
 

@@ -146,3 +146,16 @@ def test_oracle_matches_torch_chain_from_a_late_step(start_step):
             np.testing.assert_array_equal(st.m, s["exp_avg"].numpy())
             np.testing.assert_array_equal(st.v, s["exp_avg_sq"].numpy())
             assert _normwise(st.w, p.detach().numpy()) <= 1e-6
+
+
+@pytest.mark.parametrize("scale,growth", [(2.0 ** 127, 2.0), (3.0e38, 1.1), (1.7e38, 2.0),
+                                          (2.0 ** 126, 2.0), (2.0 ** -100, 0.5)])
+@pytest.mark.parametrize("found", [0.0, 1.0, float("nan")])
+def test_scaler_update_matches_torch_at_the_edges(scale, growth, found):
+    """torch._amp_update_scale_ (grad_scaler.py:549) against the oracle: growth that would
+    overflow fp32 is not applied, a NaN flag counts as found, backoff rounds through double."""
+    s = torch.tensor([scale], dtype=torch.float32)
+    t = torch.tensor([0], dtype=torch.int32)
+    torch._amp_update_scale_(s, t, torch.tensor([found]), growth, 0.5, 1)
+    o_scale, o_tracker = O.scaler_update(np.float32(scale), 0, found != 0.0, growth, 0.5, 1)
+    assert np.float32(s.item()) == o_scale and int(t.item()) == o_tracker
