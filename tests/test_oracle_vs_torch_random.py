@@ -159,3 +159,25 @@ def test_scaler_update_matches_torch_at_the_edges(scale, growth, found):
     torch._amp_update_scale_(s, t, torch.tensor([found]), growth, 0.5, 1)
     o_scale, o_tracker = O.scaler_update(np.float32(scale), 0, found != 0.0, growth, 0.5, 1)
     assert np.float32(s.item()) == o_scale and int(t.item()) == o_tracker
+
+
+@pytest.mark.parametrize("max_norm", [1.0, 0.25, 1e-3])
+@pytest.mark.parametrize("kind", ["zero", "tiny", "at_max", "large", "inf", "nan"])
+def test_clip_coefficient_matches_torch(kind, max_norm):
+    """torch.nn.utils.clip_grad_norm_ (clip_grad.py:165-174) multiplies every gradient by its
+    clamped coefficient; the oracle's coefficient times the same gradients must give the same
+    bits, including for a zero, inf or NaN total norm."""
+    g = torch.tensor([3.0, -4.0, 0.5, 1e-20], dtype=torch.float32)
+    g = {"zero": g * 0.0, "tiny": g * 1e-30, "at_max": g / float(torch.linalg.vector_norm(g)) *
+         max_norm, "large": g * 1e10,
+         "inf": torch.cat([g, torch.tensor([float("inf")])]),
+         "nan": torch.cat([g, torch.tensor([float("nan")])])}[kind]
+    p = torch.nn.Parameter(torch.zeros_like(g))
+    p.grad = g.clone()
+    norm = torch.nn.utils.clip_grad_norm_([p], max_norm)
+    coef = O.clip_coefficient(np.float32(norm.item()), max_norm)
+    with np.errstate(invalid="ignore", over="ignore"):
+        want = (g.numpy() * coef).astype(np.float32)
+    got = p.grad.numpy()
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    np.testing.assert_array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
