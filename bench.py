@@ -782,14 +782,20 @@ def _stdout_to_stderr() -> None:
 def main() -> None:
     _stdout_to_stderr()
     ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="qwen3_8b", choices=sorted(workloads.WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "torch-cuda"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gpus", type=int, default=1,
+                    help="GPUs of this node (N>1 under torchrun: one rank per GPU, ZeRO-1)")
+    ap.add_argument("--steps", type=int, default=10, help="timed steps")
+    ap.add_argument("--warmup", type=int, default=3, help="untimed steps before them")
+    ap.add_argument("--workload", default="qwen3_8b", choices=sorted(workloads.WORKLOADS),
+                    help="parameter-shape list (default: the Qwen3-8B-shaped configuration)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "torch-cuda"],
+                    help="ours: this package; reference: the reference's CPU chain on the host "
+                         "cores (rank 0); torch-cuda: torch's own fused CUDA AdamW path")
+    ap.add_argument("--e2e-steps", type=int, default=3,
+                    help="steps of the end-to-end measurement with host-resident gradients")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU baseline leg (N=1)")
     ap.add_argument("--peer-memory", action="store_true",
                     help="N>1: store the updated bf16 shards into every rank's parameters from "
                          "the update kernel (fused all-gather over NVLink peer memory)")
