@@ -18,7 +18,10 @@ betas, eps, fused=...)`` at ``train.py:359-365`` and drives it through ``zero_gr
 What is different underneath:
 
 * master weights, moments and step counters live in flat fp32 device buffers (one allocation
-  each, 256-byte aligned segments per parameter); the state entries are views into them;
+  each, 256-byte aligned segments per parameter); the state entries are views into them.  Update
+  an entry's tensors in place (``copy_``) or assign a whole new dict to ``optimizer.state[p]``
+  (copied into the buffers at the next step, which is how the reference's loaders write state);
+  rebinding a single key of an existing entry to another tensor is not seen by the kernels;
 * ``GradScaler.unscale_`` and ``clip_grad_norm_`` of this package do not rewrite gradients; they
   run one read-only statistics pass (``b2o_grad_stats``) and record the loss scale and clip
   threshold, which the update kernel (``b2o_adamw_step``) applies while it updates the state --
