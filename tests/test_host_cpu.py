@@ -83,3 +83,36 @@ def test_unsupported_variants_raise():
                 maximize=False, differentiable=False, chunk_elems=None)
     with pytest.raises(NotImplementedError):
         validate_adamw_args(**args)
+
+
+def test_tracked_state_records_every_mutation():
+    """``optimizer.state`` of the fused optimizers remembers any write from outside, so a
+    loader's assignments are copied into the flat buffers at the next step."""
+    import copy
+    import pickle
+
+    from minigpt_train_infra_b200.optim import _TrackedState
+    st = _TrackedState()
+    assert st.dirty
+    key = object()
+    mutations = [
+        lambda s: s.__setitem__(key, {"step": 1}),
+        lambda s: s.__delitem__(key),
+        lambda s: s.clear(),
+        lambda s: s.pop(key, None),
+        lambda s: s.update({key: {}}),
+        lambda s: s.setdefault(key, {}),
+        lambda s: s[object()],            # defaultdict insertion of a missing key
+        lambda s: s.popitem(),
+    ]
+    for mutate in mutations:
+        st[key] = {}
+        st.dirty = False
+        mutate(st)
+        assert st.dirty
+    st.dirty = False
+    _ = st.get(key), key in st, len(st), list(st.items())  # reads do not mark it
+    assert not st.dirty
+    # pickling and deep copies give torch's plain mapping back
+    assert type(pickle.loads(pickle.dumps(_TrackedState({1: {"a": 2}})))) is dict
+    assert copy.deepcopy(_TrackedState({1: {"a": 2}})) == {1: {"a": 2}}
