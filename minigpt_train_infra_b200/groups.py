@@ -18,27 +18,21 @@ import torch
 def build_adamw_param_groups(model: torch.nn.Module, weight_decay: float) -> list[dict[str, Any]]:
     if weight_decay < 0:
         raise ValueError("weight_decay must be non-negative")
-    decay, no_decay, decay_names, no_decay_names = [], [], [], []
-    seen: set[int] = set()
+    members: dict[str, tuple[list, list]] = {"decay": ([], []), "no_decay": ([], [])}
+    owner: dict[int, str] = {}
     for name, p in model.named_parameters():
         if not p.requires_grad:
             continue
-        if id(p) in seen:
+        if id(p) in owner:
             raise ValueError(f"Model parameter appears more than once: {name}")
-        seen.add(id(p))
-        if p.ndim >= 2:
-            decay.append(p)
-            decay_names.append(name)
-        else:
-            no_decay.append(p)
-            no_decay_names.append(name)
-    expected = {id(p) for p in model.parameters() if p.requires_grad}
-    if seen != expected:
+        owner[id(p)] = name
+        tensors, names = members["decay" if p.ndim >= 2 else "no_decay"]
+        tensors.append(p)
+        names.append(name)
+    if set(owner) != {id(p) for p in model.parameters() if p.requires_grad}:
         raise ValueError("Optimizer parameter grouping did not cover every trainable model "
                          "parameter exactly once")
-    return [
-        {"params": decay, "param_names": decay_names, "group_name": "decay",
-         "weight_decay": weight_decay},
-        {"params": no_decay, "param_names": no_decay_names, "group_name": "no_decay",
-         "weight_decay": 0.0},
-    ]
+    # key order and values as the reference writes them (they end up in checkpoints)
+    return [{"params": members[g][0], "param_names": members[g][1], "group_name": g,
+             "weight_decay": weight_decay if g == "decay" else 0.0}
+            for g in ("decay", "no_decay")]
