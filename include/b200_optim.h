@@ -156,8 +156,12 @@ int b2o_grad_stats(const b2o_tensor* tensors, int32_t n_tensors, const b2o_chunk
  * Larger plans are rejected with B2O_ERR_TOO_LARGE -- use a larger chunk_elems or
  * b2o_grad_stats.  The call allocates and frees nothing.
  *
- * The first call on a device (with that device current) looks up the array's device address
- * once (cudaGetSymbolAddress); make that first call before any stream capture.  Each call
+ * The array exists once per CUDA context that runs this library's code: for callers of the
+ * runtime API that is the device's primary context; a host that made a driver context of its own
+ * current gets that context's copy.  The call uses the array of the context current on the
+ * calling thread, whose address it looks up (cudaGetSymbolAddress) on the first call in that
+ * context and caches under the context's id; make that first call before any stream capture,
+ * and pass a `stream` of the same context.  Each call
  * clears the counters on `stream` before its kernel.  All calls share the one array and it keeps
  * the last call's contents, so calls whose kernels overlap on the GPU (different streams without
  * ordering, or different threads) race and give wrong results: order them on one stream. */

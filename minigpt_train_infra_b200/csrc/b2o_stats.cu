@@ -14,6 +14,7 @@
 //              chunk: its partial, copied by one thread -- the same value the walk gives)
 //   slot    -> per-tensor norm fp32(sqrt(sum)), total fp32(sqrt(sum of squared norms)); the
 //              same two-level structure as clip_grad.py:_get_total_norm.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -398,18 +399,62 @@ constexpr size_t kNoallocScratchBytes =
 // comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-// Device address of g_noalloc_scratch, looked up once per device on that device's first call.
-static void* noalloc_scratch_ptr(int device) {
+// A module global exists once per CUDA context, so its device address belongs to the context
+// that is current when it is looked up.  Runtime-API callers always run in the device's primary
+// context, but an FFI host may have made a context of its own current (cuCtxCreate /
+// cuCtxSetCurrent), and the array's address there is a different one.  The cache is therefore
+// keyed by the process-unique id of the current context (cuCtxGetId; ids are never reused, so a
+// destroyed context's entry cannot be mistaken for a new one).  The two driver calls are taken
+// through the runtime's entry-point query, so the library does not link libcuda itself.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+static bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+    f = nullptr;
+    q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(f);
+  });
+  if (get_current == nullptr || get_id == nullptr) return false;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of g_noalloc_scratch in the context current on the calling thread, looked up
+// once per context (for runtime-API callers: once per device, on that device's first call).
+static void* noalloc_scratch_ptr() {
+  struct Slot { unsigned long long ctx_id; void* ptr; };
   static std::mutex mu;
-  static void* cached[64] = {nullptr};
-  if (device < 0 || device >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[device] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
-    cached[device] = p;
+  static Slot cache[64];
+  static int n_cache = 0;
+  unsigned long long id = 0;
+  void* fresh = nullptr;
+  if (!current_context_id(&id)) {
+    // No context is current on this thread yet: the lookup makes the current device's primary
+    // context current, after which it can be identified.
+    if (cudaGetSymbolAddress(&fresh, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    if (!current_context_id(&id)) return fresh;  // unidentifiable context: use it uncached
   }
-  return cached[device];
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_cache; ++i)
+    if (cache[i].ctx_id == id) return cache[i].ptr;
+  if (fresh == nullptr && cudaGetSymbolAddress(&fresh, g_noalloc_scratch) != cudaSuccess)
+    return nullptr;
+  if (n_cache < 64) cache[n_cache++] = Slot{id, fresh};
+  return fresh;
 }
 
 }  // namespace b2o
@@ -425,9 +470,7 @@ extern "C" int b2o_grad_stats_noalloc(const b2o_tensor* tensors, int32_t n_tenso
   if (grad_dtype != B2O_BF16 && grad_dtype != B2O_F32) return B2O_ERR_ARG;
   if (n_chunks > B2O_NOALLOC_MAX_CHUNKS || n_slots > B2O_NOALLOC_MAX_SLOTS)
     return B2O_ERR_TOO_LARGE;
-  int device = -1;
-  if (cudaGetDevice(&device) != cudaSuccess) return B2O_ERR_CUDA;
-  void* scratch = noalloc_scratch_ptr(device);
+  void* scratch = noalloc_scratch_ptr();
   if (scratch == nullptr) return B2O_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // The counters must start at zero; the partial sums are written before they are read.

@@ -38,6 +38,7 @@ CUDA tensors only; there is no CPU path.  Not supported (raise): ``amsgrad``, ``
 
 from __future__ import annotations
 
+import warnings
 import weakref
 from collections import defaultdict
 from dataclasses import dataclass
@@ -62,6 +63,30 @@ class GradStats:
     norm: torch.Tensor           # 0-dim fp32, total L2 norm of the unscaled gradients
     loss_scale: torch.Tensor | None
     max_norm: float | None = None
+    versions: tuple = ()         # autograd version counters of the gradients after the pass
+
+
+_version_of = torch.Tensor._version.__get__
+
+STALE_STATS_MESSAGE = (
+    "gradients were modified after this package's GradScaler.unscale_() / clip_grad_norm_() "
+    "took their statistics, so the recorded loss scale, non-finite flag and norm no longer "
+    "describe them (torch.nn.utils.clip_grad_norm_, for one, rescales gradients in place: "
+    "with this package's GradScaler, clip with minigpt_train_infra_b200.clip_grad_norm_ "
+    "instead, or use torch.amp.GradScaler together with torch's clip)")
+
+
+def check_stats_current(pend: GradStats | None, versions: tuple) -> None:
+    """Raise when the gradients changed since the statistics pass of ``pend`` was launched.
+
+    This package's ``unscale_`` leaves the gradients scaled and hands the scale to the update
+    kernel; a torch ``clip_grad_norm_`` run in between multiplies them in place by
+    ``max_norm / (S * norm)`` and the kernel would then apply ``1/S`` a second time -- a step
+    clipped to ``max_norm / S`` with no error.  Every in-place write bumps a tensor's version
+    counter, so comparing the counters catches this and any other modification.
+    """
+    if pend is not None and pend.versions != versions:
+        raise RuntimeError(STALE_STATS_MESSAGE)
 
 
 def validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
@@ -146,6 +171,8 @@ class FusedAdamW(torch.optim.Optimizer):
         plans = self._prepare()
         pend = self._pending
         self._pending = None
+        if pend is not None:
+            check_stats_current(pend, self._grad_versions())
         if not plans:
             return loss
         store = self._store
@@ -300,8 +327,18 @@ class FusedAdamW(torch.optim.Optimizer):
             if not single:
                 _lib.call("b2o_finalize_norm", store.exch.data_ptr(), 1, store.n_slots,
                           out.data_ptr(), out.data_ptr() + 4, stream)
-        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale)
+        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale,
+                                  versions=self._grad_versions())
         return self._pending
+
+    def _grad_versions(self) -> tuple:
+        """Which gradient tensors the plan points at (a replaced tensor may also be at version
+        0) and the version counter of each."""
+        store = self._store
+        if store is None:
+            return ()
+        return (self._grad_key,
+                tuple(_version_of(p.grad) if p.grad is not None else -1 for p in store.params))
 
     def _owns_exactly(self, params: list[torch.Tensor]) -> bool:
         theirs = {id(p) for p in params if p.grad is not None}
@@ -560,7 +597,16 @@ class _FlatStore:
             own["step"].fill_(float(val.item() if isinstance(val, torch.Tensor) else val))
         for k in ("exp_avg", "exp_avg_sq"):
             if k in st:
-                own[k].copy_(st[k].reshape(p.shape))
+                src = st[k]
+                if isinstance(src, torch.Tensor) and src.dtype in (torch.bfloat16, torch.float16):
+                    warnings.warn(
+                        f"optimizer state '{k}' arrived as {src.dtype} for a {p.dtype} parameter; "
+                        "it was rounded to that dtype before it reached the optimizer (a loader "
+                        "that casts state to the parameter dtype, such as the reference's "
+                        "_move_optimizer_state, does this), so the fp32 moments lost their low "
+                        "bits.  Load through optimizer.load_state_dict() to keep them fp32.",
+                        RuntimeWarning, stacklevel=3)
+                own[k].copy_(src.reshape(p.shape))
         if "master_param" in own:
             if "master_param" in st:
                 own["master_param"].copy_(st["master_param"].reshape(p.shape))

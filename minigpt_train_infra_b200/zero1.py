@@ -49,7 +49,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .optim import GradStats, _REGISTRY, _round_up, validate_adamw_args
+from .optim import (GradStats, _REGISTRY, _round_up, _version_of, check_stats_current,
+                    validate_adamw_args)
 from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
 
 _ALIGN = 64
@@ -308,6 +309,10 @@ class ZeroAdamW(torch.optim.Optimizer):
         self._adopt_grads()
         pend = self._pending
         self._pending = None
+        if pend is not None:
+            # every gradient is a view of flat_grad and shares its version counter; a gradient
+            # tensor replaced since the statistics pass was copied in just now, which bumps it
+            check_stats_current(pend, (_version_of(self.flat_grad),))
         found_inf = getattr(self, "found_inf", None)
         if found_inf is not None:
             found_inf = found_inf.to(device=self.device, dtype=torch.float32)
@@ -494,7 +499,8 @@ class ZeroAdamW(torch.optim.Optimizer):
         else:
             exch = self.exch_local
         self._kernels.finalize(exch, self.world_size, self.n_slots, out)
-        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale)
+        self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale,
+                                  versions=(_version_of(self.flat_grad),))
         return self._pending
 
     def _owns_exactly(self, params) -> bool:

@@ -240,6 +240,66 @@ def test_stock_torch_gradscaler_and_clip_work_with_fused_adamw(call_unscale):
             assert float(opt.state[p]["step"]) == st.step
 
 
+@pytest.mark.parametrize("combo", ["ours+ours", "stock+ours", "ours+torch", "ours+mutate",
+                                   "ours+replace"])
+def test_scaler_and_clip_combinations(combo):
+    """train.py:485-486 calls ``scaler.unscale_`` and ``torch.nn.utils.clip_grad_norm_`` by
+    their full names, so a half-applied swap is easy to make.  This package's scaler leaves the
+    gradients scaled; torch's clip would then rescale them in place by max_norm/(S*norm) and the
+    update would apply 1/S again.  The supported pairs must match the oracle; a gradient written
+    (or replaced) after this package's statistics pass must make the step raise, before any
+    kernel runs."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    shapes = [(96, 64), (64,), (5,)]
+    w0, params = _params(shapes, torch.bfloat16, seed=11)
+    opt = FusedAdamW(params, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    for p, w in zip(params, w0):
+        opt.set_master_(p, w.to(DEV))
+    scaler_name, clip_name = combo.split("+")
+    S = 2.0 ** 12
+    sc = (GradScaler if scaler_name == "ours" else torch.amp.GradScaler)("cuda", init_scale=S)
+    sc.scale(torch.ones((), device=DEV))
+    states = [O.TensorState(w=w.numpy().copy(), m=np.zeros(w.shape, np.float32),
+                            v=np.zeros(w.shape, np.float32)) for w in w0]
+    osc = O.ScalerState(scale=np.float32(S))
+    hp = [O.GroupHP(1e-3, 0.9, 0.95, 1e-8, 0.1)]
+    store = opt._ensure_store()
+    before = [v["master_param"].clone() for v in store.views]
+    for s in range(3):
+        gs = _grads(shapes, s, torch.bfloat16, S)
+        for p, g in zip(params, gs):
+            p.grad = g.to(DEV)
+        sc.unscale_(opt)
+        if clip_name == "torch":
+            norm = torch.nn.utils.clip_grad_norm_(params, 1.0)
+        else:
+            norm = clip_grad_norm_(params, 1.0)
+        if clip_name == "mutate":
+            params[2].grad.mul_(2.0)
+        if clip_name == "replace":
+            params[1].grad = params[1].grad.clone()
+        if clip_name in ("torch", "mutate", "replace"):
+            with pytest.raises(RuntimeError, match="modified after"):
+                sc.step(opt)
+            torch.cuda.synchronize()
+            for v, b in zip(store.views, before):  # nothing was launched: state untouched
+                assert torch.equal(v["master_param"], b)
+            assert not bool(store.steps.any())
+            return
+        sc.step(opt)
+        sc.update()
+        O.optimizer_step(states, [g.float().numpy() for g in gs], hp, osc, 1.0,
+                         norm=np.float32(norm.item()))
+        assert float(sc.get_scale()) == float(osc.scale)
+        for p, st in zip(params, states):
+            m = opt.state[p]["master_param"].cpu().numpy()
+            if scaler_name == "ours":
+                np.testing.assert_array_equal(m, st.w)
+            else:  # torch's unscale_ rewrote the gradients first; the same values within 1e-6
+                assert _normwise(m, st.w) <= 1e-6
+            assert float(opt.state[p]["step"]) == st.step
+
+
 def test_parameters_without_grads_are_left_alone():
     from minigpt_train_infra_b200 import FusedAdamW
     shapes = [(32, 32), (32,)]
