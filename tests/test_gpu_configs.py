@@ -1,4 +1,4 @@
-"""Parity at the full sizes of the benchmark configurations (BASELINE configs 1-4).
+"""Parity at the full sizes of the benchmark configurations (BASELINE configs 1-5).
 
 At these sizes the reference's own CPU norm is inaccurate (torch accumulates fp32 norms in fp32:
 -4.3% at 2**28 elements), so the checks are: the oracle fed the kernel's own norm must agree bit
@@ -249,3 +249,114 @@ def test_config4_qwen3_1_7b_skip_is_free_and_step_matches():
         np.testing.assert_array_equal(vv["master_param"].view(-1)[ix].cpu().numpy(), w2)
         np.testing.assert_array_equal(vv["exp_avg"].view(-1)[ix].cpu().numpy(), m2)
         np.testing.assert_array_equal(vv["exp_avg_sq"].view(-1)[ix].cpu().numpy(), v2)
+
+
+def _fp64_norm_chunked(grads, inv_scale: float, piece: int = 1 << 26) -> float:
+    """_fp64_norm computed in pieces, so the fp64 temporaries stay small next to 131 GB of
+    state."""
+    norms = []
+    for g in grads:
+        flat = g.view(-1)
+        acc = 0.0
+        for a in range(0, flat.numel(), piece):
+            x = (flat[a:a + piece].float() * inv_scale).double()
+            acc += float((x * x).sum())
+        norms.append(np.float32(math.sqrt(acc)))
+    return float(O.total_norm(norms))
+
+
+def test_config5_qwen3_8b_skip_is_free_and_step_matches():
+    """Config 5 on one GPU, the benchmark's headline workload: Qwen3-8B-shaped (399 tensors,
+    8,190,735,360 params, ~131 GB of state), loss scale 2**15, clip 1.0, stored step 999 so the
+    update uses step 1000.  A step with an inf leaves every state word and bf16 parameter
+    unchanged (exact integer checksums), and the next step matches the oracle given the kernel's
+    norm on 4096 seeded samples of every tensor; the norm is within 2 ulp of an fp64 norm."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    torch.cuda.empty_cache()
+    shapes = workloads.shapes("qwen3_8b")
+    assert len(shapes) == 399 and workloads.n_params("qwen3_8b") == 8_190_735_360
+    gen = torch.Generator(device=DEV).manual_seed(5)
+    params = [torch.nn.Parameter(torch.empty(s, dtype=torch.bfloat16, device=DEV))
+              for _, s, _ in shapes]
+    groups = [{"params": [p for p, (_, _, g) in zip(params, shapes) if g == 0],
+               "weight_decay": 0.1},
+              {"params": [p for p, (_, _, g) in zip(params, shapes) if g == 1],
+               "weight_decay": 0.0}]
+    opt = FusedAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+    st = opt._ensure_store()
+    opt._sync_state()
+    for buf, std, absval in ((st.master, 0.02, False), (st.exp_avg, 1e-3, False),
+                             (st.exp_avg_sq, 1e-6, True)):
+        for a in range(0, buf.numel(), 1 << 28):
+            part = buf[a:a + (1 << 28)]
+            part.normal_(0, 1, generator=gen)
+            if absval:
+                part.abs_()
+            part.mul_(std)
+    st.steps.fill_(999.0)
+    with torch.no_grad():
+        for slot, p in enumerate(st.params):
+            p.copy_(st.views[slot]["master_param"])
+    S = 2.0 ** 15
+    grads = [torch.empty(s, dtype=torch.bfloat16, device=DEV) for _, s, _ in shapes]
+    for p, g in zip(params, grads):
+        flat = g.view(-1)
+        for a in range(0, flat.numel(), 1 << 27):
+            part = flat[a:a + (1 << 27)]
+            part.copy_(torch.randn(part.numel(), generator=gen, device=DEV) * 1e-3 * S)
+        p.grad = g
+    sc = GradScaler("cuda", init_scale=S, growth_interval=2000, backoff_factor=0.5)
+    sc.scale(torch.ones((), device=DEV))
+
+    def piecewise_sum(t, piece=1 << 27):
+        """Exact integer sum of a tensor's words, in pieces (the int64 widening of a whole
+        32 GB buffer would not fit beside the state)."""
+        flat = t.view(-1)
+        return sum(int(flat[a:a + piece].sum(dtype=torch.int64))
+                   for a in range(0, flat.numel(), piece))
+
+    def checksum():
+        acc = [piecewise_sum(t.view(torch.int32))
+               for t in (st.master, st.exp_avg, st.exp_avg_sq, st.steps)]
+        acc.append(sum(piecewise_sum(p.detach().view(torch.int16)) for p in params))
+        return acc
+
+    before = checksum()
+    grads[200].view(-1)[12345] = float("inf")
+    sc.unscale_(opt); clip_grad_norm_(params, 1.0); sc.step(opt); sc.update()
+    assert checksum() == before
+    assert float(sc.get_scale()) == S / 2
+    assert {float(s["step"]) for s in opt.state.values()} == {999.0}
+    grads[200].view(-1)[12345] = 0.0
+    samp = {}
+    for slot, p in enumerate(st.params):
+        n = p.numel()
+        ix = torch.randint(0, n, (min(n, 4096),), generator=gen, device=DEV)
+        v = st.views[slot]
+        samp[slot] = (ix, v["master_param"].view(-1)[ix].cpu().numpy(),
+                      v["exp_avg"].view(-1)[ix].cpu().numpy(),
+                      v["exp_avg_sq"].view(-1)[ix].cpu().numpy(),
+                      _bits(p.grad.view(-1)[ix]))
+    sc.unscale_(opt)
+    norm = clip_grad_norm_(params, 1.0)
+    sc.step(opt)
+    sc.update()
+    nrm = np.float32(norm.item())
+    assert abs(float(nrm) - _fp64_norm_chunked(grads, 1.0 / (S / 2))) <= 2 * np.spacing(nrm)
+    inv = O.inv_scale_of(S / 2)
+    coef = O.clip_coefficient(nrm, 1.0)
+    assert coef < 1.0  # clipping is active at this size
+    n_decay = len(groups[0]["params"])
+    for slot, (ix, w, m, v, gb) in samp.items():
+        g = (O.unscale(O.bf16_bits_to_f32(gb), inv) * coef).astype(np.float32)
+        hp = O.GroupHP(3e-4, 0.9, 0.95, 1e-8, 0.1 if slot < n_decay else 0.0)
+        w2, m2, v2 = O.adamw_update(w, m, v, g, hp, 1000.0)
+        vv = st.views[slot]
+        np.testing.assert_array_equal(vv["master_param"].view(-1)[ix].cpu().numpy(), w2)
+        np.testing.assert_array_equal(vv["exp_avg"].view(-1)[ix].cpu().numpy(), m2)
+        np.testing.assert_array_equal(vv["exp_avg_sq"].view(-1)[ix].cpu().numpy(), v2)
+        np.testing.assert_array_equal(_bits(st.params[slot].view(-1)[ix]),
+                                      O.f32_to_bf16_bits(w2))
+    assert {float(s["step"]) for s in opt.state.values()} == {1000.0}
+    del samp, grads, params, opt, st
+    torch.cuda.empty_cache()

@@ -251,11 +251,14 @@ def test_scaler_and_clip_combinations(combo):
     kernel runs."""
     from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
     shapes = [(96, 64), (64,), (5,)]
-    w0, params = _params(shapes, torch.bfloat16, seed=11)
+    scaler_name, clip_name = combo.split("+")
+    # torch's own unscale_ has no bf16 CUDA kernel, so its pairing runs on fp32 parameters (the
+    # reference's fp16-autocast mode keeps fp32 parameters too)
+    dtype = torch.float32 if scaler_name == "stock" else torch.bfloat16
+    w0, params = _params(shapes, dtype, seed=11)
     opt = FusedAdamW(params, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
     for p, w in zip(params, w0):
         opt.set_master_(p, w.to(DEV))
-    scaler_name, clip_name = combo.split("+")
     S = 2.0 ** 12
     sc = (GradScaler if scaler_name == "ours" else torch.amp.GradScaler)("cuda", init_scale=S)
     sc.scale(torch.ones((), device=DEV))
@@ -264,9 +267,10 @@ def test_scaler_and_clip_combinations(combo):
     osc = O.ScalerState(scale=np.float32(S))
     hp = [O.GroupHP(1e-3, 0.9, 0.95, 1e-8, 0.1)]
     store = opt._ensure_store()
-    before = [v["master_param"].clone() for v in store.views]
+    before = [v.get("master_param", q).detach().clone()
+              for v, q in zip(store.views, store.params)]
     for s in range(3):
-        gs = _grads(shapes, s, torch.bfloat16, S)
+        gs = _grads(shapes, s, dtype, S)
         for p, g in zip(params, gs):
             p.grad = g.to(DEV)
         sc.unscale_(opt)
@@ -292,7 +296,7 @@ def test_scaler_and_clip_combinations(combo):
                          norm=np.float32(norm.item()))
         assert float(sc.get_scale()) == float(osc.scale)
         for p, st in zip(params, states):
-            m = opt.state[p]["master_param"].cpu().numpy()
+            m = opt.state[p].get("master_param", p.detach()).float().cpu().numpy()
             if scaler_name == "ours":
                 np.testing.assert_array_equal(m, st.w)
             else:  # torch's unscale_ rewrote the gradients first; the same values within 1e-6
