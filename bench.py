@@ -38,10 +38,10 @@ L2_BYTES = 126 * 2 ** 20
 ADAMW_BYTES = 28   # read g(2)+w,m,v(12); write w,m,v(12)+bf16 param(2)
 STATS_BYTES = 2    # read g
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes per parameter of one adamw_kernel launch, from ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum = 940.43 MB + 882.66 MB over 2**26 params; profiles/
-# adamw_kernel_flat_2_26_full.md).  The full workload is too large to capture under the profiler's
-# size rule, so the per-parameter figure of the small capture is scaled by the params per launch.
+# DRAM bytes per parameter of one adamw_kernel launch, from an ncu capture of the flat 2**26
+# workload (dram__bytes_read.sum + dram__bytes_write.sum = 940.43 MB + 882.66 MB over 2**26
+# params).  The full workload is too large to capture under the profiler's size rule, so the
+# per-parameter figure of the small capture is scaled by the params per launch.
 NCU_TRAFFIC_BYTES_PER_PARAM = (940.429824e6 + 882.656768e6) / 2 ** 26
 LR, BETAS, EPS, WD, CLIP = 3e-4, (0.9, 0.95), 1e-8, 0.1, 1.0
 SCALES = {"qwen3_8b": 2.0 ** 15}
@@ -240,6 +240,226 @@ def run_cpu_baseline(shape_list, scale: float, std: float, steps: int = 3, warmu
 
 
 # ------------------------------------------------------------------------------------------
+# parity leg: one more step through the public API, after the timed steps, checked against the
+# oracle.  The oracle is the checker here, never the thing timed.
+# ------------------------------------------------------------------------------------------
+
+PARITY_SAMPLES = 4096
+
+
+def _owned_slices(opt, ws: int) -> list[dict]:
+    """Every tensor range this rank updates, as flat 1-D views of its state, gradient and bf16
+    parameter, with its step slot and hyper-parameter group."""
+    out = []
+    if ws > 1:
+        g = opt.geom
+        for slot, lo, hi in g.local_ranges():
+            if hi <= lo:
+                continue
+            la, lb = lo - g.lo, hi - g.lo
+            out.append({"slot": slot, "group": opt._slot_group[slot], "flat_lo": lo,
+                        "master": opt.master[la:lb], "exp_avg": opt.exp_avg[la:lb],
+                        "exp_avg_sq": opt.exp_avg_sq[la:lb], "grad": opt.flat_grad[lo:hi],
+                        "param": opt.flat_param[lo:hi], "steps": opt.steps})
+        return out
+    store = opt._store
+    gid = {id(p): gi for gi, grp in enumerate(opt.param_groups) for p in grp["params"]}
+    for slot, p in enumerate(store.params):
+        v = store.views[slot]
+        out.append({"slot": slot, "group": gid[id(p)], "flat_lo": None,
+                    "master": v["master_param"].view(-1), "exp_avg": v["exp_avg"].view(-1),
+                    "exp_avg_sq": v["exp_avg_sq"].view(-1), "grad": p.grad.view(-1),
+                    "param": p.detach().view(-1), "steps": store.steps})
+    return out
+
+
+def _bits16(t: torch.Tensor):
+    return t.contiguous().view(torch.int16).cpu().numpy().view("uint16")
+
+
+def _piecewise_int_sum(t: torch.Tensor, piece: int = 1 << 27) -> int:
+    """Exact integer sum of a tensor's words, in pieces (no full-size int64 temporary)."""
+    dt = torch.int16 if t.element_size() == 2 else torch.int32
+    flat = t.view(dt).view(-1)
+    return sum(int(flat[a:a + piece].sum(dtype=torch.int64)) for a in range(0, flat.numel(), piece))
+
+
+def _fp64_norm(grads, inv_scale: float, piece: int = 1 << 26) -> float:
+    """The statistics' two-level norm with the sums in fp64: fp32(sqrt(sum x^2)) per tensor, then
+    the norm of those, x = fp32(g * inv_scale)."""
+    import numpy as np
+    from oracle import adamw_oracle as O
+    norms = []
+    for g in grads:
+        flat = g.reshape(-1)
+        acc = 0.0
+        for a in range(0, flat.numel(), piece):
+            x = (flat[a:a + piece].float() * inv_scale).double()
+            acc += float((x * x).sum())
+        norms.append(np.float32(math.sqrt(acc)))
+    return float(O.total_norm(norms))
+
+
+def _state_checksum(opt, ws: int) -> list[int]:
+    """Exact checksums of every state word this rank owns, its step counters and its copy of the
+    bf16 parameters."""
+    if ws > 1:
+        bufs = [opt.master, opt.exp_avg, opt.exp_avg_sq, opt.steps, opt.flat_param]
+    else:
+        st = opt._store
+        bufs = [st.master, st.exp_avg, st.exp_avg_sq, st.steps] + [p.detach() for p in st.params]
+    return [_piecewise_int_sum(b) for b in bufs]
+
+
+def parity_check(opt, scaler, step_params, ws: int, rank: int, seed: int = 0) -> dict:
+    """Two more steps through the public API (unscale_ -> clip_grad_norm_ -> step -> update, and
+    the bf16 parameter exchange at N>1), checked against the oracle:
+
+    * a clean step: on every rank, PARITY_SAMPLES seeded elements of every tensor range the rank
+      owns (all of a shorter range) -- master, exp_avg and exp_avg_sq bit-exact against the
+      oracle fed the kernel's global norm; at N>1 every rank's copy of the bf16 parameters at
+      every rank's samples bit-exact against the oracle's bf16 rounding (the gathered
+      parameters), and each rank's own bf16 shard equal to bf16(master) word for word; rank 0
+      checks the global norm against an fp64 norm of the whole gradient (within 2 ulp);
+    * a step with +inf at one element of the last rank's range: found_inf is 1 on every rank,
+      every state word, step counter and bf16 parameter is unchanged on every rank, and the loss
+      scale is halved.
+
+    Returns the summary on rank 0 (None elsewhere).  Every rank issues the same collectives."""
+    import numpy as np
+    from minigpt_train_infra_b200 import clip_grad_norm_
+    from oracle import adamw_oracle as O
+    dist = torch.distributed if ws > 1 else None
+    device = scaler._scale.device
+    sync = torch.cuda.synchronize if device.type == "cuda" else (lambda: None)
+    slices = _owned_slices(opt, ws)
+    gen = torch.Generator().manual_seed(1000 * seed + 17 * rank + 1)
+    before = []
+    for sl in slices:
+        n = sl["master"].numel()
+        k = min(n, PARITY_SAMPLES)
+        ix = torch.randint(0, n, (k,), generator=gen).to(device)
+        before.append({"ix": ix, "w": sl["master"][ix].cpu().numpy(),
+                       "m": sl["exp_avg"][ix].cpu().numpy(),
+                       "v": sl["exp_avg_sq"][ix].cpu().numpy(), "g": _bits16(sl["grad"][ix]),
+                       "step": float(sl["steps"][sl["slot"]])})
+    scale0 = float(scaler.get_scale())
+    sync()
+
+    def api_step():
+        scaler.unscale_(opt)
+        norm = clip_grad_norm_(step_params, CLIP)
+        found = next(iter(scaler._per_optimizer_states[id(opt)]["found_inf_per_device"]
+                          .values())).clone()
+        scaler.step(opt)
+        scaler.update()
+        if ws > 1 and opt.defer_param_gather:
+            opt.gather_params()
+        sync()
+        return float(norm), float(found)
+
+    norm, found = api_step()
+    norm32 = np.float32(norm)
+    inv = O.inv_scale_of(scale0)
+    coef = O.clip_coefficient(norm32, CLIP)
+    groups = opt.param_groups
+    mism = 0
+    max_ulp = 0
+    checked = 0
+    expect_pos, expect_bits = [], []
+    for sl, b in zip(slices, before):
+        grp = groups[sl["group"]]
+        hp = O.GroupHP(grp["lr"], grp["betas"][0], grp["betas"][1], grp["eps"],
+                       grp["weight_decay"])
+        g = (O.unscale(O.bf16_bits_to_f32(b["g"]), inv) * coef).astype(np.float32)
+        w2, m2, v2 = O.adamw_update(b["w"], b["m"], b["v"], g, hp, b["step"] + 1.0)
+        for key, want in (("master", w2), ("exp_avg", m2), ("exp_avg_sq", v2)):
+            got = sl[key][b["ix"]].cpu().numpy()
+            d = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+            mism += int(np.count_nonzero(d))
+            max_ulp = max(max_ulp, int(d.max()) if d.size else 0)
+        pbits = O.f32_to_bf16_bits(w2)
+        mism += int(np.count_nonzero(_bits16(sl["param"][b["ix"]]) != pbits))
+        checked += len(b["w"])
+        if sl["flat_lo"] is not None:
+            expect_pos.append(b["ix"].cpu().numpy() + sl["flat_lo"])
+            expect_bits.append(pbits)
+    gathered_checked = gathered_mism = shard_mism = 0
+    if ws > 1:
+        # each rank's own bf16 shard is bf16(master), word for word ...
+        own = opt.flat_param[opt.geom.lo:opt.geom.hi]
+        for a in range(0, own.numel(), 1 << 27):
+            shard_mism += int((own[a:a + (1 << 27)].view(torch.int16) !=
+                               opt.master[a:a + (1 << 27)].to(torch.bfloat16).view(torch.int16))
+                              .sum())
+        # ... and every rank holds every rank's updated bf16 values at the sampled positions
+        mine = (np.concatenate(expect_pos) if expect_pos else np.zeros(0, np.int64),
+                np.concatenate(expect_bits) if expect_bits else np.zeros(0, np.uint16))
+        allv = [None] * ws
+        dist.all_gather_object(allv, mine)
+        for pos, bits in allv:
+            if len(pos) == 0:
+                continue
+            got = _bits16(opt.flat_param[torch.from_numpy(pos).to(device)])
+            gathered_mism += int(np.count_nonzero(got != bits))
+            gathered_checked += len(pos)
+    norm_ref = None
+    if rank == 0:
+        grads = [p.grad for p in step_params]
+        norm_ref = _fp64_norm(grads, float(inv))
+    norm_ulp = None if norm_ref is None else abs(float(norm32) - norm_ref) / float(
+        np.spacing(norm32))
+
+    # the skip: +inf at one element of the last rank's range
+    sums0 = _state_checksum(opt, ws)
+    inj = None
+    if rank == ws - 1:
+        sl = slices[-1]
+        pos = min(17, sl["grad"].numel() - 1)
+        inj = (sl["grad"], pos, sl["grad"][pos].clone())
+        sl["grad"][pos] = float("inf")
+    scale1 = float(scaler.get_scale())
+    _, found_skip = api_step()
+    scale2 = float(scaler.get_scale())
+    sums1 = _state_checksum(opt, ws)
+    if inj is not None:
+        inj[0][inj[1]] = inj[2]
+        sync()
+    local = torch.tensor([mism, max_ulp, checked, gathered_checked, gathered_mism, shard_mism,
+                          found_skip != 1.0, sums0 != sums1, scale2 != scale1 * 0.5,
+                          found != 0.0], dtype=torch.float64, device=device)
+    if ws > 1:
+        parts = [torch.empty_like(local) for _ in range(ws)]
+        dist.all_gather(parts, local)
+        tot = torch.stack(parts).cpu().numpy()
+    else:
+        tot = local.cpu().numpy()[None, :]
+    if rank != 0:
+        return None
+    ok = bool(tot[:, [0, 4, 5, 6, 7, 8, 9]].sum() == 0 and norm_ulp is not None and
+              norm_ulp <= 2.0)
+    return {
+        "ok": ok,
+        "samples_checked": int(tot[:, 2].sum()),
+        "state_words_checked": int(3 * tot[:, 2].sum()),
+        "state_words_mismatched": int(tot[:, 0].sum()),
+        "max_ulp_diff": int(tot[:, 1].max()),
+        "gathered_bf16_checked": int(tot[:, 3].sum()),
+        "gathered_bf16_mismatched": int(tot[:, 4].sum()),
+        "own_shard_bf16_vs_master_mismatched": int(tot[:, 5].sum()),
+        "norm": {"kernel": float(norm32), "fp64_reference": norm_ref,
+                 "ulp_diff": None if norm_ulp is None else round(norm_ulp, 3)},
+        "clean_step_found_inf_zero_on_every_rank": bool(tot[:, 9].sum() == 0),
+        "skip": {"inf_on_rank": ws - 1, "found_inf_on_every_rank": bool(tot[:, 6].sum() == 0),
+                 "state_and_steps_unchanged_on_every_rank": bool(tot[:, 7].sum() == 0),
+                 "scale_halved_on_every_rank": bool(tot[:, 8].sum() == 0),
+                 "scale": [scale1, scale2]},
+        "how": (f"{PARITY_SAMPLES} seeded samples of every owned tensor range per rank, after "
+                "the timed steps; oracle fed the kernel's global norm; bit-exact compare"),
+    }
+
+
+# ------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------
 
@@ -248,6 +468,30 @@ def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
+
+
+def make_zero_opt(groups, pg, rank: int, std: float, scale: float, peer_memory: bool,
+                  defer_param_gather: bool):
+    """ZeroAdamW over ``groups`` with the seeded state of the benchmark: each rank's shard of
+    master ~ N(0,0.02), m ~ N(0,1e-3), v = |N(0,1)|*1e-6 (rank-specific seeds), step 999, and the
+    same bf16 gradients N(0,std)*scale on every rank."""
+    from minigpt_train_infra_b200 import ZeroAdamW
+    opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=pg,
+                    defer_param_gather=defer_param_gather, peer_memory=peer_memory)
+    fill_seeded(opt.master, 1 + 101 * rank, 0.02)
+    fill_seeded(opt.exp_avg, 2 + 101 * rank, 1e-3)
+    fill_seeded(opt.exp_avg_sq, 3 + 101 * rank, 1e-6, absval=True)
+    opt.steps.fill_(999.0)
+    with torch.no_grad():
+        opt.owned_param_shard().copy_(opt.master)
+    if peer_memory:
+        # the fused broadcast writes tensor ranges only from the first step on; start every
+        # rank's copy equal with one ordinary all-gather
+        torch.distributed.all_gather_into_tensor(opt.flat_param, opt.owned_param_shard(),
+                                                 group=pg)
+    opt.gather_params()
+    fill_seeded(opt.flat_grad, 7, std * scale)
+    return opt
 
 
 def run_ours(args) -> None:
@@ -273,17 +517,8 @@ def run_ours(args) -> None:
               {"params": [p for p, g in zip(params, gids) if g == 1], "weight_decay": 0.0}]
     groups = [g for g in groups if g["params"]]
     if ws > 1:
-        from minigpt_train_infra_b200 import ZeroAdamW
-        opt = ZeroAdamW(groups, lr=LR, betas=BETAS, eps=EPS, process_group=pg,
-                        defer_param_gather=True, peer_memory=args.peer_memory)
-        fill_seeded(opt.master, 1 + 101 * rank, 0.02)
-        fill_seeded(opt.exp_avg, 2 + 101 * rank, 1e-3)
-        fill_seeded(opt.exp_avg_sq, 3 + 101 * rank, 1e-6, absval=True)
-        opt.steps.fill_(999.0)
-        with torch.no_grad():
-            opt.owned_param_shard().copy_(opt.master)
-        opt.gather_params()
-        fill_seeded(opt.flat_grad, 7, std * scale)
+        opt = make_zero_opt(groups, pg, rank, std, scale, peer_memory=args.peer_memory,
+                            defer_param_gather=True)
         grads = opt.make_flat_grads_()
         step_params = opt.managed_params()
         params = step_params
@@ -399,10 +634,26 @@ def run_ours(args) -> None:
     if ws > 1:
         launches_per_step += 1  # finalize of the exchanged partials
 
+    # parity: two more steps through the same API after the timed ones, checked by the oracle
+    leg = "single_gpu" if ws == 1 else ("zero1_peer_memory" if args.peer_memory else
+                                        "zero1_nccl_allgather")
+    parity = {leg: parity_check(opt, scaler, step_params, ws, rank)}
+
     # end-to-end through the public API with host-resident gradients
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, opt, scaler, step_params, params, grads, device, P, pg)
+
+    # N>1: the full step with the bf16 all-gather fused into the update, timed and checked in
+    # the same run (the NCCL leg's buffers are released first: both do not fit at once)
+    peer_leg = None
+    if ws > 1 and not args.peer_memory and not args.no_peer_leg:
+        del opt, grads, step_params, params, scaler
+        opt = None
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        peer_leg = run_peer_leg(args, shape_list, P, scale, std, device, pg, ws, rank)
+        parity["zero1_peer_memory"] = peer_leg.pop("parity")
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -454,12 +705,81 @@ def run_ours(args) -> None:
         }
         if ws > 1:
             line["allgather"] = allgather
+            line["full_step"] = {"zero1_nccl_allgather": allgather}
+            if peer_leg is not None:
+                line["full_step"]["zero1_peer_memory"] = peer_leg
+        line["parity"] = {"ok": all(v is not None and v["ok"] for v in parity.values()),
+                          **parity}
         emit_result(line)
     if pg is not None:
-        if hasattr(opt, "close"):
+        if opt is not None and hasattr(opt, "close"):
             opt.close()
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def _nvlink_bound(P_padded: int, P_local: int, ws: int) -> dict:
+    """Lower bound of a full ZeRO-1 step at N ranks: every rank must receive the other ranks'
+    updated bf16 shards, 2 * P * (N-1)/N bytes over its NVLink at the measured 770 GB/s per
+    direction, and must stream its own shard's 30 bytes per parameter through HBM."""
+    peak, _ = hbm_peak()
+    recv = 2 * P_padded * (ws - 1) / ws
+    nvlink_ms = recv / 770e9 * 1e3
+    hbm_ms = (ADAMW_BYTES + STATS_BYTES) * P_local / (peak * 1e9) * 1e3
+    return {"recv_bytes_per_rank": int(recv), "nvlink_ms": round(nvlink_ms, 3),
+            "hbm_ms": round(hbm_ms, 3), "bound_ms": round(max(nvlink_ms, hbm_ms), 3),
+            "bound": "nvlink" if nvlink_ms >= hbm_ms else "hbm"}
+
+
+def run_peer_leg(args, shape_list, P: int, scale: float, std: float, device, pg, ws: int,
+                 rank: int) -> dict:
+    """The ZeRO-1 step with the bf16 all-gather fused into the update (``peer_memory=True``):
+    the AdamW kernel stores every updated bf16 value into every rank's parameter buffer over
+    NVLink (plain 16-byte stores, no multicast), then a one-element all-reduce orders the ranks.
+    Timed as the full step -- statistics, norm exchange, update with broadcast, ordering, scaler
+    update -- with CUDA events, max over ranks; then checked by the parity leg."""
+    import torch.distributed as dist
+    from minigpt_train_infra_b200 import GradScaler, clip_grad_norm_
+    params, gids = make_model_params(shape_list, device)
+    groups = [{"params": [p for p, g in zip(params, gids) if g == 0], "weight_decay": WD},
+              {"params": [p for p, g in zip(params, gids) if g == 1], "weight_decay": 0.0}]
+    groups = [g for g in groups if g["params"]]
+    opt = make_zero_opt(groups, pg, rank, std, scale, peer_memory=True,
+                        defer_param_gather=False)
+    opt.make_flat_grads_()
+    step_params = opt.managed_params()
+    scaler = GradScaler("cuda", init_scale=scale, growth_interval=2000, backoff_factor=0.5)
+    scaler.scale(torch.ones((), device=device))
+
+    def one_step():
+        scaler.unscale_(opt)
+        clip_grad_norm_(step_params, CLIP)
+        scaler.step(opt)
+        scaler.update()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one_step()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    bound = _nvlink_bound(opt.geom.padded, opt.local_numel(), ws)
+    out = {"ms": round(ms, 4), "gparams_s": round(P / (ms / 1e3) / 1e9, 3), **bound,
+           "frac_of_bound": round(bound["bound_ms"] / ms, 4),
+           "note": "statistics + norm exchange + AdamW with the bf16 broadcast fused in (16-byte "
+                   "peer stores over legacy CUDA IPC mappings) + ordering all-reduce + scaler "
+                   "update, per step; max over ranks"}
+    out["parity"] = parity_check(opt, scaler, step_params, ws, rank, seed=1)
+    opt.close()
+    return out
 
 
 def fused_broadcast_report(opt, P, ws, ms_per_step, adamw_ms):
@@ -501,7 +821,10 @@ def time_allgather(args, opt, one_step, device, P, ws):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ag_ms, full_ms = (float(x) / k for x in t.tolist())
     recv = 2 * opt.geom.padded * (ws - 1) / ws  # bytes each rank receives per gather
+    bound = _nvlink_bound(opt.geom.padded, opt.local_numel(), ws)
     return {"ms": round(ag_ms, 4), "recv_bytes_per_rank": int(recv),
+            "full_step_bound_ms": bound["bound_ms"], "full_step_bound": bound["bound"],
+            "full_step_frac_of_bound": round(bound["bound_ms"] / full_ms, 4),
             "gbs_per_rank": round(recv / (ag_ms / 1e3) / 1e9, 1),
             "nvlink_peak_gbs": 770.0,
             "frac_of_nvlink": round(recv / (ag_ms / 1e3) / 1e9 / 770.0, 4),
@@ -646,8 +969,8 @@ def run_dp_step(args) -> None:
     """The complete data-parallel ZeRO-1 step, N ranks with different local gradients:
     gradient reduce-scatter -> statistics -> norm exchange -> AdamW -> bf16 parameter gather,
     either with NCCL collectives around the kernels (``--dp-step nccl``) or with the fused
-    peer-memory kernels (``--dp-step fused``).  Prints its own JSON line; the driver's default
-    line is run_ours."""
+    peer-memory kernels (``--dp-step fused``).  Prints its own JSON line (the default run is
+    run_ours)."""
     import datetime
     import torch.distributed as dist
     ws, rank, local = dist_env()
@@ -799,6 +1122,9 @@ def main() -> None:
     ap.add_argument("--peer-memory", action="store_true",
                     help="N>1: store the updated bf16 shards into every rank's parameters from "
                          "the update kernel (fused all-gather over NVLink peer memory)")
+    ap.add_argument("--no-peer-leg", action="store_true",
+                    help="N>1: skip the second leg that times and checks the step with the bf16 "
+                         "all-gather fused into the update over peer memory")
     ap.add_argument("--graph", action="store_true",
                     help="N=1: capture the step in a CUDA graph and time its replays")
     ap.add_argument("--dp-step", choices=["nccl", "fused"], default=None,

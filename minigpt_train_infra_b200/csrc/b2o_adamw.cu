@@ -100,6 +100,35 @@ struct Broadcast {
   int my_rank;
 };
 
+// Stores one updated quad (4 bf16 = 8 bytes; quad q of a chunk's nq quads, at `dst` in this
+// rank's buffer) at the same offset of every other rank's buffer.  The quads of lanes 2k and 2k+1
+// are adjacent (q even and q + 1), so together they are 16 bytes on a 16-byte boundary: when both
+// exist the pair swaps them with a shuffle and each lane stores the 16 bytes to half of the peers
+// (even lane: peers 0, 2, 4, ... of the CTA's rotated list; odd lane: 1, 3, 5, ...).  A quad
+// whose partner is past the end of the chunk goes to every peer as 8 bytes.  Both lanes of a
+// pair evaluate the same condition (q_odd < nq), so the pair shuffle always has both lanes.
+__device__ __forceinline__ void broadcast_quad(const Broadcast& bc, char* const* s_peer,
+                                               const uint16_t* dst, uint2 pq, int64_t q,
+                                               int64_t nq, int lane) {
+  const int64_t byte = reinterpret_cast<const char*>(dst) - bc.my_base;
+  const int n_peers = bc.n_ranks - 1;
+  if ((q ^ 1) < nq) {
+    const unsigned pair = 3u << (lane & ~1);
+    const unsigned ox = __shfl_xor_sync(pair, pq.x, 1);
+    const unsigned oy = __shfl_xor_sync(pair, pq.y, 1);
+    const int odd = lane & 1;
+    const uint4 v = odd ? make_uint4(ox, oy, pq.x, pq.y) : make_uint4(pq.x, pq.y, ox, oy);
+    const int64_t base = odd ? byte - 8 : byte;
+#pragma unroll
+    for (int j = 0; j < B2O_MAX_PEERS - 1; j += 2) {
+      const int k = j + odd;
+      if (k < n_peers) __stcs(reinterpret_cast<uint4*>(s_peer[k] + base), v);
+    }
+  } else {
+    for (int k = 0; k < n_peers; ++k) __stcs(reinterpret_cast<uint2*>(s_peer[k] + byte), pq);
+  }
+}
+
 template <class G, bool BF16_PARAM, int Q, bool BCAST = false, bool DEV_HP = false>
 __global__ void __launch_bounds__(kThreads, B2O_ADAMW_MIN_CTAS)
 adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
@@ -110,6 +139,17 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
              const b2o_group* __restrict__ dev_groups = nullptr) {
   if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step: no traffic at all
   __shared__ int is_last;
+  // The other ranks' buffers in the order this CTA stores to them: starting after this rank and
+  // rotated by the CTA index, so the stores in flight spread over all peers at any moment.
+  __shared__ char* s_peer[B2O_MAX_PEERS];
+  if (BCAST) {
+    const int n_peers = bc.n_ranks - 1;
+    if (threadIdx.x < n_peers) {
+      const int j = int((threadIdx.x + blockIdx.x) % unsigned(n_peers));
+      s_peer[threadIdx.x] = bc.peers.p[(bc.my_rank + 1 + j) % bc.n_ranks];
+    }
+    __syncthreads();
+  }
   const float inv = inv_scale_of(loss_scale);
   const float coef = norm_p ? clip_coefficient(*norm_p, max_norm) : 1.0f;
   if (clip_coef_out && blockIdx.x == 0 && threadIdx.x == 0) *clip_coef_out = coef;
@@ -212,13 +252,7 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
               pq.x = pack_bf16x2(wf[0], wf[1]);
               pq.y = pack_bf16x2(wf[2], wf[3]);
               __stcs(reinterpret_cast<uint2*>(pp + e), pq);
-              if (BCAST) {
-                const int64_t byte = reinterpret_cast<const char*>(pp + e) - bc.my_base;
-#pragma unroll
-                for (int r = 0; r < B2O_MAX_PEERS; ++r)
-                  if (r < bc.n_ranks && r != bc.my_rank)
-                    __stcs(reinterpret_cast<uint2*>(bc.peers.p[r] + byte), pq);
-              }
+              if (BCAST) broadcast_quad(bc, s_peer, pp + e, pq, q, nq, lane);
             }
           }
         }
@@ -238,8 +272,8 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
         pp[e] = b;
         if (BCAST) {
           const int64_t byte = reinterpret_cast<const char*>(pp + e) - bc.my_base;
-          for (int r = 0; r < bc.n_ranks; ++r)
-            if (r != bc.my_rank) *reinterpret_cast<uint16_t*>(bc.peers.p[r] + byte) = b;
+          for (int j = 0; j < bc.n_ranks - 1; ++j)
+            *reinterpret_cast<uint16_t*>(s_peer[j] + byte) = b;
         }
       }
     }

@@ -1,6 +1,6 @@
 """``bench.py``'s output contract, checked on a CPU-only host through its reference arm (the
-reference's CPU chain needs no GPU): exactly one JSON line on stdout with the keys and units the
-round driver reads, the metric of BASELINE.json, and silence from ranks other than 0."""
+reference's CPU chain needs no GPU): exactly one JSON line on stdout with the keys and units its
+readers expect, the metric of BASELINE.json, and silence from ranks other than 0."""
 
 from __future__ import annotations
 
