@@ -110,11 +110,14 @@ int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups, in
                     int64_t chunk_elems, int32_t grad_dtype, b2o_chunk* chunks,
                     int64_t chunk_cap, int64_t* n_chunks);
 
-/* Bytes of device workspace the stats pass needs for a plan (all calls of one optimizer share
- * it): per-chunk partial sums, the per-slot exchange vector and two completion counters. */
+/* Bytes of device workspace a plan needs (the statistics and update passes of one plan share
+ * it): completion and chunk-claim counters, one completion counter and one folded sum per
+ * tensor entry (n_slots bounds the entries), one partial sum per chunk and the per-slot
+ * exchange vector. */
 size_t b2o_workspace_bytes(int64_t n_chunks, int32_t n_slots);
 
-/* Zero the counters of a freshly allocated workspace (cudaMemsetAsync on `stream`). */
+/* Zero a freshly allocated workspace of `bytes` bytes (cudaMemsetAsync on `stream`).  The
+ * passes return every counter to zero when they finish, so this is needed once. */
 int b2o_workspace_init(void* workspace, size_t bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------- */

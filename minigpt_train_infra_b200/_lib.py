@@ -132,10 +132,17 @@ def check(fn: str, status: int) -> None:
         raise B2OError(fn, status, text)
 
 
+_FUNCS: dict = {}
+
+
 def call(fn: str, *args) -> int:
     """Call an entry point returning b2o_status and raise on failure."""
-    status = getattr(load(), fn)(*args)
-    check(fn, status)
+    f = _FUNCS.get(fn)
+    if f is None:
+        f = _FUNCS[fn] = getattr(load(), fn)
+    status = f(*args)
+    if status:
+        check(fn, status)
     return status
 
 

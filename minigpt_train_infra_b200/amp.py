@@ -80,7 +80,8 @@ class GradScaler(torch.amp.GradScaler):
         if new_scale is not None:
             return super().update(new_scale)
         _scale, _growth_tracker = self._check_scale_growth_tracker("update")
-        found_infs = [f.to(device=_scale.device, non_blocking=True)
+        dev = _scale.device
+        found_infs = [f if f.device == dev else f.to(device=dev, non_blocking=True)
                       for state in self._per_optimizer_states.values()
                       for f in state["found_inf_per_device"].values()]
         if len(found_infs) == 0:
@@ -88,8 +89,9 @@ class GradScaler(torch.amp.GradScaler):
         found = found_infs[0]
         for f in found_infs[1:]:
             found = found + f
-        if _scale.device.type == "cuda":
-            found = found.to(torch.float32).contiguous()
+        if dev.type == "cuda":
+            if found.dtype != torch.float32:
+                found = found.to(torch.float32)
             _lib.call("b2o_scaler_update", _scale.data_ptr(), _growth_tracker.data_ptr(),
                       found.data_ptr(), float(self._growth_factor), float(self._backoff_factor),
                       int(self._growth_interval), stream_ptr(_scale.device))

@@ -61,12 +61,12 @@ extern "C" const char* b2o_status_string(int status) {
   }
 }
 
-extern "C" int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups,
-                               int32_t n_slots, int64_t chunk_elems, int32_t grad_dtype,
-                               b2o_chunk* chunks, int64_t chunk_cap, int64_t* n_chunks) {
+// Validates the table, fills chunk_begin / chunk_count / flags of every entry and, when `chunks`
+// is not NULL, writes the chunks of `chunk_elems` elements (the last of a tensor shorter).
+static int plan_walk(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups, int32_t n_slots,
+                     int64_t chunk_elems, int32_t grad_dtype, b2o_chunk* chunks,
+                     int64_t chunk_cap, int64_t* n_chunks) {
   if (!n_chunks || n_tensors < 0 || (n_tensors > 0 && !tensors)) return B2O_ERR_ARG;
-  if (chunk_elems <= 0 || chunk_elems % B2O_VEC != 0 || chunk_elems > (int64_t(1) << 30))
-    return B2O_ERR_ARG;
   if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS || n_slots < n_tensors) return B2O_ERR_ARG;
   if (grad_dtype != B2O_BF16 && grad_dtype != B2O_F32) return B2O_ERR_ARG;
   std::unordered_set<int32_t> seen;
@@ -104,16 +104,23 @@ extern "C" int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n
   return B2O_OK;
 }
 
+extern "C" int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups,
+                               int32_t n_slots, int64_t chunk_elems, int32_t grad_dtype,
+                               b2o_chunk* chunks, int64_t chunk_cap, int64_t* n_chunks) {
+  if (chunk_elems <= 0 || chunk_elems % B2O_VEC != 0 || chunk_elems > (int64_t(1) << 30))
+    return B2O_ERR_ARG;
+  return plan_walk(tensors, n_tensors, n_groups, n_slots, chunk_elems, grad_dtype, chunks,
+                   chunk_cap, n_chunks);
+}
+
 extern "C" size_t b2o_workspace_bytes(int64_t n_chunks, int32_t n_slots) {
   if (n_chunks < 0 || n_slots < 0) return 0;
-  return ws_counter_bytes() + size_t(n_chunks) * sizeof(double) +
-         size_t(n_slots + 1) * sizeof(double);
+  return ws_total_bytes(n_chunks, n_slots);
 }
 
 extern "C" int b2o_workspace_init(void* workspace, size_t bytes, void* stream) {
   if (!workspace || bytes < ws_counter_bytes()) return B2O_ERR_ARG;
-  return cudaMemsetAsync(workspace, 0, ws_counter_bytes(), static_cast<cudaStream_t>(stream)) ==
-                 cudaSuccess
+  return cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? B2O_OK
              : B2O_ERR_CUDA;
 }

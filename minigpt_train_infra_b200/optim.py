@@ -38,6 +38,7 @@ CUDA tensors only; there is no CPU path.  Not supported (raise): ``amsgrad``, ``
 
 from __future__ import annotations
 
+import operator
 import warnings
 import weakref
 from collections import defaultdict
@@ -63,10 +64,24 @@ class GradStats:
     norm: torch.Tensor           # 0-dim fp32, total L2 norm of the unscaled gradients
     loss_scale: torch.Tensor | None
     max_norm: float | None = None
-    versions: tuple = ()         # autograd version counters of the gradients after the pass
+    versions: tuple = ()         # gradient signature (addresses and version counters) after it
+    plans: Any = None            # the plans the pass ran on, reused by the update
 
 
 _version_of = torch.Tensor._version.__get__
+_data_ptr = torch.Tensor.data_ptr
+_dtype_of = operator.attrgetter("dtype")
+
+
+def grad_signature(grads: list) -> tuple:
+    """The gradient tensors' addresses and autograd version counters, built with C-level maps
+    (this runs twice per step).  A missing gradient is recorded by its position."""
+    try:
+        return (tuple(map(_data_ptr, grads)), tuple(map(_version_of, grads)))
+    except TypeError:  # a parameter without a gradient
+        act = [g for g in grads if g is not None]
+        return (tuple(map(_data_ptr, act)), tuple(map(_version_of, act)),
+                tuple(i for i, g in enumerate(grads) if g is None))
 
 STALE_STATS_MESSAGE = (
     "gradients were modified after this package's GradScaler.unscale_() / clip_grad_norm_() "
@@ -137,6 +152,9 @@ class FusedAdamW(torch.optim.Optimizer):
         self._hp_dev: torch.Tensor | None = None
         self._pending: GradStats | None = None
         self._active_ids: frozenset | None = None
+        self._owns_cache: tuple | None = None
+        self._group_cache: tuple | None = None
+        self._last_grads: list = []
         self.state = _TrackedState(self.state)
         _REGISTRY.add(self)
 
@@ -168,17 +186,25 @@ class FusedAdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        plans = self._prepare()
         pend = self._pending
         self._pending = None
         if pend is not None:
-            check_stats_current(pend, self._grad_versions())
+            # the statistics pass of this iteration planned these gradients; reuse its plans
+            # unless the gradients (or the plans) changed since, which makes its results stale
+            self._sync_state()
+            check_stats_current(pend, grad_signature([p.grad for p in self._store.params]))
+            plans = pend.plans
+            if plans and plans is not self._plans:
+                raise RuntimeError(STALE_STATS_MESSAGE)
+        else:
+            plans = self._prepare()
         if not plans:
             return loss
         store = self._store
         device = store.device
         found_inf = getattr(self, "found_inf", None)
-        if found_inf is not None:
+        if found_inf is not None and (found_inf.dtype != torch.float32 or
+                                      found_inf.device != device):
             found_inf = found_inf.to(device=device, dtype=torch.float32, non_blocking=True)
         loss_scale = pend.loss_scale if pend is not None else None
         grad_scale = getattr(self, "grad_scale", None)
@@ -328,26 +354,28 @@ class FusedAdamW(torch.optim.Optimizer):
                 _lib.call("b2o_finalize_norm", store.exch.data_ptr(), 1, store.n_slots,
                           out.data_ptr(), out.data_ptr() + 4, stream)
         self._pending = GradStats(found_inf=out[0], norm=out[1], loss_scale=loss_scale,
-                                  versions=self._grad_versions())
+                                  versions=grad_signature(self._last_grads) if plans else
+                                  (grad_signature([p.grad for p in self._store.params])
+                                   if self._store is not None else ()),
+                                  plans=plans)
         return self._pending
 
-    def _grad_versions(self) -> tuple:
-        """Which gradient tensors the plan points at (a replaced tensor may also be at version
-        0) and the version counter of each."""
-        store = self._store
-        if store is None:
-            return ()
-        return (self._grad_key,
-                tuple(_version_of(p.grad) if p.grad is not None else -1 for p in store.params))
-
     def _owns_exactly(self, params: list[torch.Tensor]) -> bool:
+        key = tuple(map(id, params))
+        pending = self._pending is not None and self._active_ids is not None
+        cached = self._owns_cache
+        if pending and cached is not None and cached[0] is self._active_ids and cached[1] == key:
+            return True  # the same parameter list as last time, against the same plan
         theirs = {id(p) for p in params if p.grad is not None}
-        if self._pending is not None and self._active_ids is not None:
+        if pending:
             # the statistics pass of this iteration just matched the plan to these gradients
             mine = self._active_ids
         else:
             mine = {id(p) for g in self.param_groups for p in g["params"] if p.grad is not None}
-        return mine == theirs
+        owned = mine == theirs
+        if owned and pending and len(theirs) == len(key):
+            self._owns_cache = (self._active_ids, key)
+        return owned
 
     def set_master_(self, param: torch.Tensor, master: torch.Tensor) -> None:
         """Overwrite the fp32 master (and the bf16 copy) of one parameter, e.g. from fp32
@@ -370,16 +398,17 @@ class FusedAdamW(torch.optim.Optimizer):
     # ------------------------------------------------------------------------------------
 
     def _group_array(self) -> np.ndarray:
-        n = len(self.param_groups)
-        if n > _lib.MAX_GROUPS:
+        """Every group's (lr, beta1, beta2, eps, weight_decay) as the kernel's group records;
+        rebuilt only when a value changed (lr usually changes every step)."""
+        key = tuple((float(g["lr"]), *map(float, g["betas"]), float(g["eps"]),
+                     float(g["weight_decay"])) for g in self.param_groups)
+        cached = self._group_cache
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        if len(key) > _lib.MAX_GROUPS:
             raise ValueError(f"at most {_lib.MAX_GROUPS} param groups are supported")
-        arr = np.zeros(n, dtype=_lib.GROUP_DTYPE)
-        for i, g in enumerate(self.param_groups):
-            lr = g["lr"]
-            if isinstance(lr, torch.Tensor):
-                lr = float(lr)
-            b1, b2 = g["betas"]
-            arr[i] = (float(lr), float(b1), float(b2), float(g["eps"]), float(g["weight_decay"]))
+        arr = np.array(list(key), dtype=_lib.GROUP_DTYPE)
+        self._group_cache = (key, arr)
         return arr
 
     def _all_params(self) -> list[torch.Tensor]:
@@ -453,7 +482,29 @@ class FusedAdamW(torch.optim.Optimizer):
         self._sync_state()
         params = store.params
         grads = [p.grad for p in params]
-        if any(g is None for g in grads):
+        self._last_grads = grads
+        try:
+            gptr = tuple(map(_data_ptr, grads))
+        except TypeError:  # some parameters have no gradient
+            gptr = None
+        if gptr is not None:
+            active = None
+            pptr = tuple(map(_data_ptr, params))
+            key = self._plan_key
+            if key is not None and key[2] is None and key[0] == pptr:
+                # the planned parameters, every one with a gradient: the common case
+                if gptr == self._grad_key:
+                    return self._plans
+                if tuple(map(_dtype_of, grads)) == key[1]:
+                    if torch.cuda.is_current_stream_capturing():
+                        raise RuntimeError("gradient tensors changed since the last step; call "
+                                           "prepare_replay() (or one eager step) before "
+                                           "capturing")
+                    self._refresh_grads(grads, gptr)
+                    return self._plans
+            skey = (pptr, tuple(map(_dtype_of, grads)), None)
+            act_grads = grads
+        else:
             active = [(slot, p, g) for slot, (p, g) in enumerate(zip(params, grads))
                       if g is not None]
             if not active:
@@ -462,11 +513,6 @@ class FusedAdamW(torch.optim.Optimizer):
                     tuple(g.dtype for _, _, g in active), tuple(s for s, _, _ in active))
             gptr = tuple(g.data_ptr() for _, _, g in active)
             act_grads = [g for _, _, g in active]
-        else:
-            active = None
-            skey = (tuple(map(_data_ptr, params)), tuple(g.dtype for g in grads), None)
-            gptr = tuple(map(_data_ptr, grads))
-            act_grads = grads
         if skey == self._plan_key:
             if gptr != self._grad_key:
                 if torch.cuda.is_current_stream_capturing():
@@ -595,18 +641,19 @@ class _FlatStore:
         if "step" in st:
             val = st["step"]
             own["step"].fill_(float(val.item() if isinstance(val, torch.Tensor) else val))
+        for k in ("exp_avg", "exp_avg_sq", "master_param"):
+            src = st.get(k)
+            if isinstance(src, torch.Tensor) and src.dtype in (torch.bfloat16, torch.float16):
+                warnings.warn(
+                    f"optimizer state '{k}' arrived as {src.dtype} for a {p.dtype} parameter: it "
+                    "was rounded to that dtype before it reached the optimizer (a loader that "
+                    "casts state to the parameter dtype, such as the reference's "
+                    "_move_optimizer_state, does this), so its fp32 value lost its low bits.  "
+                    "Load through optimizer.load_state_dict() to keep optimizer state in fp32.",
+                    RuntimeWarning, stacklevel=3)
         for k in ("exp_avg", "exp_avg_sq"):
             if k in st:
-                src = st[k]
-                if isinstance(src, torch.Tensor) and src.dtype in (torch.bfloat16, torch.float16):
-                    warnings.warn(
-                        f"optimizer state '{k}' arrived as {src.dtype} for a {p.dtype} parameter; "
-                        "it was rounded to that dtype before it reached the optimizer (a loader "
-                        "that casts state to the parameter dtype, such as the reference's "
-                        "_move_optimizer_state, does this), so the fp32 moments lost their low "
-                        "bits.  Load through optimizer.load_state_dict() to keep them fp32.",
-                        RuntimeWarning, stacklevel=3)
-                own[k].copy_(src.reshape(p.shape))
+                own[k].copy_(st[k].reshape(p.shape))
         if "master_param" in own:
             if "master_param" in st:
                 own["master_param"].copy_(st["master_param"].reshape(p.shape))
@@ -617,9 +664,6 @@ class _FlatStore:
 
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
-
-
-_data_ptr = torch.Tensor.data_ptr
 
 
 class _TrackedState(defaultdict):

@@ -178,5 +178,11 @@ def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device | None = None) -> int:
+    """The current CUDA stream of ``device`` as a raw ``cudaStream_t`` value."""
+    if _raw_stream is not None and device is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream

@@ -54,6 +54,7 @@ from .optim import (GradStats, _REGISTRY, _round_up, _version_of, check_stats_cu
 from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
 
 _ALIGN = 64
+_INSTANCES = 0  # ZeroAdamW objects built in this process (names a group in the membership store)
 
 
 class ShardGeometry:
@@ -166,7 +167,8 @@ class ZeroAdamW(torch.optim.Optimizer):
                  differentiable: bool = False, fused: bool | None = None,
                  process_group=None, chunk_elems: int | None = DEFAULT_CHUNK_ELEMS,
                  defer_param_gather: bool = False, peer_memory: bool = False,
-                 reduce_grads: bool = False, grad_average: bool = True, _kernels=None):
+                 reduce_grads: bool = False, grad_average: bool = True, membership_store=None,
+                 _kernels=None):
         validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
                             chunk_elems)
         defaults = dict(lr=lr, betas=(float(betas[0]), float(betas[1])), eps=eps,
@@ -195,6 +197,15 @@ class ZeroAdamW(torch.optim.Optimizer):
         self._kernels = _kernels if _kernels is not None else CudaKernels()
         if _kernels is None and self.device.type != "cuda":
             raise RuntimeError("ZeroAdamW runs on CUDA devices only; there is no CPU path")
+        # Host-side membership check (opt-in): a rank that leaves between steps announces it in
+        # this torch.distributed Store, and every rank looks before its step's first collective,
+        # so the others end their next step with an error instead of waiting in a collective.
+        # All ranks build their ZeroAdamW objects in the same order, so the count of objects
+        # built in this process names the same group on every rank.
+        global _INSTANCES
+        _INSTANCES += 1
+        self._members = membership_store
+        self._members_key = f"b2o_zero1/{_INSTANCES}/left"
         self.peer_memory = bool(peer_memory) and self.world_size > 1
         self.reduce_grads = bool(reduce_grads)
         self.grad_scale_factor = 1.0 / self.world_size if grad_average else 1.0
@@ -274,6 +285,24 @@ class ZeroAdamW(torch.optim.Optimizer):
                 dist.all_gather_into_tensor(self.flat_param, self.owned_param_shard(),
                                             group=self.pg)
 
+    def announce_leave(self) -> None:
+        """Called by a rank that is about to leave the group between steps (needs
+        ``membership_store``).  Call it after its last step and before a last barrier with the
+        other ranks, then exit: the barrier orders the announcement before their next step,
+        whose membership check then raises before any collective or kernel is issued."""
+        if self._members is None:
+            raise RuntimeError("announce_leave needs ZeroAdamW(membership_store=...)")
+        self._members.add(self._members_key, 1)
+
+    def _check_members(self) -> None:
+        if self._members is not None:
+            left = self._members.add(self._members_key, 0)
+            if left:
+                raise RuntimeError(
+                    f"{left} rank(s) of this ZeroAdamW group announced that they left; the step "
+                    "was not started (no collective or kernel issued).  Rebuild the process "
+                    "group and the optimizer, e.g. from consolidated_state_dict()")
+
     def _barrier(self) -> None:
         """Stream-ordered rendezvous: returns (on the stream) once every rank's earlier work
         on its stream has completed.  A one-element all-reduce, no host blocking."""
@@ -306,6 +335,8 @@ class ZeroAdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        if self._pending is None:
+            self._check_members()
         self._adopt_grads()
         pend = self._pending
         self._pending = None
@@ -473,6 +504,7 @@ class ZeroAdamW(torch.optim.Optimizer):
 
     @torch.no_grad()
     def _grad_stats(self, loss_scale: torch.Tensor | None) -> GradStats:
+        self._check_members()
         self._adopt_grads()
         if loss_scale is not None:
             loss_scale = loss_scale.to(device=self.device, dtype=torch.float32)

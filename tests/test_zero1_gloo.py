@@ -242,6 +242,66 @@ def test_rank_failing_before_exchange_gives_bounded_error(tmp_path):
     assert float(secs) < 60.0
 
 
+def _worker_announced_leave(rank, world, init_file, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [here, os.path.dirname(here)]
+    from zero_oracle_backend import OracleKernels
+    from minigpt_train_infra_b200 import GradScaler, clip_grad_norm_
+    from minigpt_train_infra_b200.zero1 import ZeroAdamW
+    _, params = _make(rank, world, torch.float32, init_file, timeout_s=30)
+    store = dist.FileStore(str(init_file) + ".members", world)
+    opt = ZeroAdamW(params, **HP, membership_store=store, _kernels=OracleKernels())
+    scaler = GradScaler("cpu", init_scale=2.0 ** 12)
+    scaler.scale(torch.ones(()))
+    for step in range(3):
+        if step == 2 and rank == world - 1:
+            dist.destroy_process_group()
+            os._exit(0)
+        for p, g in zip(params, _grads(step, torch.float32, 2.0 ** 12)):
+            p.grad = g
+        t0 = time.time()
+        try:
+            scaler.unscale_(opt)
+            clip_grad_norm_(opt.managed_params(), 1.0)
+            scaler.step(opt)
+            scaler.update()
+        except RuntimeError as e:
+            with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+                f.write(f"{step}\n{time.time() - t0:.3f}\n{e}\n")
+            os._exit(0)
+        if step == 1:
+            if rank == world - 1:
+                opt.announce_leave()
+            dist.barrier()
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write("no error\n")
+    os._exit(0)
+
+
+@pytest.mark.slow
+def test_announced_leave_makes_the_next_step_raise_before_any_collective(tmp_path):
+    """A rank that leaves between steps announces it in the membership store before the last
+    barrier; the other ranks' next step raises at once (no collective issued), at 3 ranks."""
+    ctx = mp.get_context("spawn")
+    world = 3
+    procs = [ctx.Process(target=_worker_announced_leave,
+                         args=(r, world, str(tmp_path / "rdzv"), str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    for r in range(world - 1):
+        step, secs, msg = (tmp_path / f"rank{r}.txt").read_text().split("\n", 2)
+        assert step == "2" and float(secs) < 5.0, (step, secs, msg)
+        assert "announced that they left" in msg
+
+
 # --------------------------------------------------------------------------------------------
 # consolidated checkpoints and resharding (world 2 -> world 3)
 # --------------------------------------------------------------------------------------------

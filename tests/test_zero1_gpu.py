@@ -264,3 +264,52 @@ def test_dp_reduce_scatter_step_matches_one_gpu_on_mean_grads(tmp_path, peer_mem
                 assert np.max(d) <= 2 * 4 * 1.5e-3 + 1e-3
                 assert np.mean(d <= 2 ** -7 * np.max(np.abs(w)) + 1e-12) >= 0.98
             off += (n + 63) // 64 * 64
+
+
+@needs_world
+def test_rank_leaving_between_steps_ends_the_survivors_next_step_with_an_error(tmp_path):
+    """Failure detection over NCCL without a GPU fault.  Two child processes on two GPUs run
+    ZeroAdamW steps with NVLS off and no peer memory.  After two completed steps the second rank
+    announces in the rendezvous store that it leaves, joins a barrier (nothing of either rank in
+    flight), destroys its process group and exits.  The survivor's third step must end with an
+    error at once -- raised by the membership check before any collective or kernel -- rather
+    than wait in a collective that can never complete."""
+    import re
+    import socket
+    import subprocess
+    import sys
+    import time
+    from pathlib import Path
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    worker = Path(__file__).with_name("zero_leave_worker.py")
+    timeout_s = 10
+    procs = [subprocess.Popen([sys.executable, str(worker), str(r), "2", str(port), str(tmp_path),
+                               str(timeout_s)], env=env, stdout=subprocess.PIPE,
+                              stderr=subprocess.STDOUT, text=True) for r in range(2)]
+    deadline = time.time() + 150
+    outs, ended = [], []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=max(1.0, deadline - time.time()))
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            logs = {f.name: f.read_text() for f in sorted(tmp_path.glob("rank*.log"))}
+            pytest.fail(f"a rank was still running at the test's deadline (hang): {logs}")
+        outs.append(out)
+        ended.append(time.time())
+    log0 = (tmp_path / "rank0.log").read_text()
+    log1 = (tmp_path / "rank1.log").read_text()
+    assert procs[1].returncode == 0 and "left" in log1, outs[1][-2000:]
+    assert "step 1 done" in log0 and "step 2 start" in log0, log0
+    assert "step 2 done" not in log0 and "all steps done" not in log0, (log0, outs[0][-3000:])
+    assert procs[0].returncode == 3, (procs[0].returncode, outs[0][-3000:])
+    err = next(ln for ln in log0.splitlines() if " step 2 error " in ln)
+    assert re.search(r"announced that they left", err), err
+    started = float(next(ln.split()[0] for ln in log0.splitlines() if ln.endswith("step 2 start")))
+    assert float(err.split()[0]) - started <= 5.0, (err, started)
+    assert "announced" in log1
