@@ -111,9 +111,8 @@ int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n_groups, in
                     int64_t chunk_cap, int64_t* n_chunks);
 
 /* Bytes of device workspace a plan needs (the statistics and update passes of one plan share
- * it): completion and chunk-claim counters, one completion counter and one folded sum per
- * tensor entry (n_slots bounds the entries), one partial sum per chunk and the per-slot
- * exchange vector. */
+ * it): completion and chunk-claim counters, one partial sum per chunk and the per-slot exchange
+ * vector. */
 size_t b2o_workspace_bytes(int64_t n_chunks, int32_t n_slots);
 
 /* Zero a freshly allocated workspace of `bytes` bytes (cudaMemsetAsync on `stream`).  The

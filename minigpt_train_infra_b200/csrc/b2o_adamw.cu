@@ -382,7 +382,7 @@ extern "C" int b2o_adamw_step_bcast(const b2o_tensor* tensors, int32_t n_tensors
   for (int i = 0; i < n_groups; ++i) ga.g[i] = groups[i];
   return launch_adamw_bcast(static_cast<cudaStream_t>(stream), tensors, n_tensors, chunks,
                             n_chunks, ga, steps, found_inf, loss_scale, norm, max_norm,
-                            carve_workspace(workspace, 0, 0), grad_dtype, bc);
+                            carve_workspace(workspace, 0), grad_dtype, bc);
 }
 
 extern "C" int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors,
@@ -397,7 +397,7 @@ extern "C" int b2o_adamw_step(const b2o_tensor* tensors, int32_t n_tensors,
   if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS) return B2O_ERR_ARG;
   GroupArgs ga{};
   for (int i = 0; i < n_groups; ++i) ga.g[i] = groups[i];
-  Workspace ws = carve_workspace(workspace, 0, 0);
+  Workspace ws = carve_workspace(workspace, n_chunks);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf16p = param_dtype == B2O_BF16;
   if (param_dtype != B2O_BF16 && param_dtype != B2O_F32) return B2O_ERR_ARG;
@@ -433,7 +433,7 @@ extern "C" int b2o_adamw_step_dev(const b2o_tensor* tensors, int32_t n_tensors,
   if (n_groups <= 0 || n_groups > B2O_MAX_GROUPS) return B2O_ERR_ARG;
   if (param_dtype != B2O_BF16 && param_dtype != B2O_F32) return B2O_ERR_ARG;
   const GroupArgs ga{};
-  Workspace ws = carve_workspace(workspace, 0, 0);
+  Workspace ws = carve_workspace(workspace, n_chunks);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool bf16p = param_dtype == B2O_BF16;
   if (grad_dtype == B2O_BF16)

@@ -148,16 +148,9 @@ struct PeerPtrs {
 };
 
 // ---------------------------------------------------------------------------------------------
-// Workspace layout (b2o_workspace_bytes):
-//   [counters: 16 x uint32]
-//   [tensor_done: n_slots x uint32, padded to 8 bytes]  chunks of each table entry finished
-//   [tensor_sum: n_slots x double]                      folded sum of squares of each entry
-//   [chunk partials: n_chunks x double]
-//   [exchange: (n_slots + 1) x double]
-// The counters are the completion tickets of the two passes, the non-finite flag and the
-// chunk-claim counters; whoever takes a counter's last ticket returns it to zero, so a
-// workspace zeroed once stays ready for every later launch.  A table has at most n_slots
-// entries, so n_slots bounds the per-entry arrays.
+// Workspace layout (b2o_workspace_bytes): [counters: 8 x uint32][chunk partials: n_chunks x
+// double][exchange: (n_slots + 1) x double].  The counters are the completion tickets of the
+// two passes and the non-finite flag; each pass's last CTA returns its counter to zero.
 // ---------------------------------------------------------------------------------------------
 
 struct Workspace {
@@ -166,21 +159,13 @@ struct Workspace {
   unsigned int* adamw_done;
   unsigned int* adamw_tile;  // next chunk to hand out when the update pass schedules dynamically
   unsigned int* stats_tile;  // the same for the statistics pass
-  unsigned int* tensor_done;
-  double* tensor_sum;
   double* chunk_sums;
   double* exch;
 };
 
-__host__ __device__ constexpr size_t ws_counter_bytes() { return 64; }
+__host__ __device__ inline size_t ws_counter_bytes() { return 64; }
 
-// Bytes from the start of the workspace to the end of tensor_done: what must be zero before a
-// statistics launch that does not rely on the previous launch having cleaned up.
-__host__ __device__ constexpr size_t ws_zeroed_bytes(int64_t n_slots) {
-  return ws_counter_bytes() + (size_t(n_slots) * 4 + 7) / 8 * 8;
-}
-
-__host__ __device__ inline Workspace carve_workspace(void* ws, int64_t n_chunks, int64_t n_slots) {
+__host__ __device__ inline Workspace carve_workspace(void* ws, int64_t n_chunks) {
   Workspace w;
   unsigned int* c = static_cast<unsigned int*>(ws);
   w.stats_done = c + 0;
@@ -188,17 +173,9 @@ __host__ __device__ inline Workspace carve_workspace(void* ws, int64_t n_chunks,
   w.adamw_done = c + 2;
   w.adamw_tile = c + 3;
   w.stats_tile = c + 4;
-  char* base = static_cast<char*>(ws);
-  w.tensor_done = reinterpret_cast<unsigned int*>(base + ws_counter_bytes());
-  w.tensor_sum = reinterpret_cast<double*>(base + ws_zeroed_bytes(n_slots));
-  w.chunk_sums = w.tensor_sum + n_slots;
+  w.chunk_sums = reinterpret_cast<double*>(static_cast<char*>(ws) + ws_counter_bytes());
   w.exch = w.chunk_sums + n_chunks;
   return w;
-}
-
-__host__ __device__ constexpr size_t ws_total_bytes(int64_t n_chunks, int64_t n_slots) {
-  return ws_zeroed_bytes(n_slots) + sizeof(double) * (size_t(n_slots) + size_t(n_chunks) +
-                                                      size_t(n_slots) + 1);
 }
 
 }  // namespace b2o

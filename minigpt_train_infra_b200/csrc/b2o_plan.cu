@@ -115,7 +115,8 @@ extern "C" int b2o_plan_chunks(b2o_tensor* tensors, int32_t n_tensors, int32_t n
 
 extern "C" size_t b2o_workspace_bytes(int64_t n_chunks, int32_t n_slots) {
   if (n_chunks < 0 || n_slots < 0) return 0;
-  return ws_total_bytes(n_chunks, n_slots);
+  return ws_counter_bytes() + size_t(n_chunks) * sizeof(double) +
+         size_t(n_slots + 1) * sizeof(double);
 }
 
 extern "C" int b2o_workspace_init(void* workspace, size_t bytes, void* stream) {

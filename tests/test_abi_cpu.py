@@ -120,9 +120,7 @@ def test_planner_rejects_bad_arguments():
 
 def test_workspace_size_formula():
     lib = _lib.load()
-    # counters, per-tensor counters (3 x 4 bytes padded to 16), per-tensor sums, chunk
-    # partials, exchange vector
-    assert lib.b2o_workspace_bytes(10, 3) == 64 + 16 + 8 * 3 + 8 * 10 + 8 * 4
+    assert lib.b2o_workspace_bytes(10, 3) == 64 + 8 * 10 + 8 * 4
     assert lib.b2o_workspace_bytes(-1, 3) == 0
 
 
