@@ -38,6 +38,7 @@ CUDA tensors only; there is no CPU path.  Not supported (raise): ``amsgrad``, ``
 
 from __future__ import annotations
 
+import functools
 import operator
 import warnings
 import weakref
@@ -48,6 +49,7 @@ from typing import Any
 
 import numpy as np
 import torch
+from torch.optim import optimizer as _torch_optimizer
 
 from . import _lib
 from .plan import DEFAULT_CHUNK_ELEMS, ChunkPlan, Entry, dtype_code, stream_ptr
@@ -102,6 +104,26 @@ def check_stats_current(pend: GradStats | None, versions: tuple) -> None:
     """
     if pend is not None and pend.versions != versions:
         raise RuntimeError(STALE_STATS_MESSAGE)
+
+
+def hooked_step(func):
+    """The wrapper torch.optim.Optimizer puts around every subclass's ``step``
+    (``Optimizer.profile_hook_step``: step pre/post hooks and a profiler range), used only when
+    a hook is registered or the profiler runs; otherwise the step is called directly, which
+    saves that wrapper's fixed cost on every step of a small model."""
+    slow = torch.optim.Optimizer.profile_hook_step(func)
+
+    @functools.wraps(func)
+    def wrapper(self, *args, **kwargs):
+        if (self._optimizer_step_pre_hooks or self._optimizer_step_post_hooks
+                or _torch_optimizer._global_optimizer_pre_hooks
+                or _torch_optimizer._global_optimizer_post_hooks
+                or torch._C._autograd._profiler_enabled()):
+            return slow(self, *args, **kwargs)
+        return func(self, *args, **kwargs)
+
+    wrapper.hooked = True  # torch.optim.Optimizer then leaves it as it is
+    return wrapper
 
 
 def validate_adamw_args(lr, betas, eps, weight_decay, amsgrad, maximize, differentiable,
@@ -174,13 +196,15 @@ class FusedAdamW(torch.optim.Optimizer):
             group.setdefault("fused", None)
             group.setdefault("decoupled_weight_decay", True)
 
-    @torch.no_grad()
+    @hooked_step
     def step(self, closure=None):
         """One AdamW update of every parameter that has a gradient.
 
         Applies the pending unscale factor and clip coefficient recorded by this package's
         ``GradScaler.unscale_`` / ``clip_grad_norm_`` and skips the whole update (step counters
-        included) when ``self.found_inf`` -- set by ``GradScaler.step`` -- is non-zero.
+        included) when ``self.found_inf`` -- set by ``GradScaler.step`` -- is non-zero.  No
+        autograd-recorded operation runs here (the kernels write through raw pointers, state
+        loads copy under no_grad), so the step needs no ``torch.no_grad`` context of its own.
         """
         loss = None
         if closure is not None:
@@ -326,9 +350,9 @@ class FusedAdamW(torch.optim.Optimizer):
     # Hooks used by GradScaler / clip_grad_norm_ of this package
     # ------------------------------------------------------------------------------------
 
-    @torch.no_grad()
     def _grad_stats(self, loss_scale: torch.Tensor | None) -> GradStats:
-        """Run the read-only statistics pass over the current gradients (no host sync)."""
+        """Run the read-only statistics pass over the current gradients (no host sync; no
+        autograd-recorded operation)."""
         plans = self._prepare()
         store = self._store
         device = store.device if store is not None else torch.device("cuda",

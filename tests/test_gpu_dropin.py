@@ -339,3 +339,36 @@ def test_rejected_configurations():
         opt.step()
     with pytest.raises(ValueError):
         FusedAdamW([q], lr=-1.0)
+
+
+def test_step_hooks_and_profiler_range_as_torch_provides_them():
+    """torch.optim.Optimizer wraps every step with pre/post hooks and a profiler range; the
+    fused optimizer keeps both (it skips the wrapper's cost only when neither is in use)."""
+    from minigpt_train_infra_b200 import FusedAdamW
+    shapes = [(32, 16), (16,)]
+    _, params = _params(shapes, torch.float32, seed=3)
+    opt = FusedAdamW(params, lr=1e-3)
+    calls = []
+    pre = opt.register_step_pre_hook(lambda o, a, k: calls.append(("pre", o is opt)))
+    post = opt.register_step_post_hook(lambda o, a, k: calls.append(("post", o is opt)))
+    for p, g in zip(params, _grads(shapes, 0, torch.float32)):
+        p.grad = g.to(DEV)
+    opt.step()
+    assert calls == [("pre", True), ("post", True)]
+    pre.remove()
+    post.remove()
+    opt.step()
+    assert len(calls) == 2
+    from torch.optim.optimizer import register_optimizer_step_pre_hook
+    glob = register_optimizer_step_pre_hook(lambda o, a, k: calls.append(("global", o is opt)))
+    try:
+        opt.step()
+    finally:
+        glob.remove()
+    assert calls[-1] == ("global", True)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+        opt.step()
+    names = {e.key for e in prof.key_averages()}
+    assert "Optimizer.step#FusedAdamW.step" in names
+    torch.cuda.synchronize()
+    assert float(opt.state[params[0]]["step"]) == 4.0
