@@ -313,3 +313,81 @@ def test_rank_leaving_between_steps_ends_the_survivors_next_step_with_an_error(t
     started = float(next(ln.split()[0] for ln in log0.splitlines() if ln.endswith("step 2 start")))
     assert float(err.split()[0]) - started <= 5.0, (err, started)
     assert "announced" in log1
+
+
+def _reshard_worker(rank, world, port, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [here, os.path.dirname(here)]
+    import torch.distributed as dist
+    from minigpt_train_infra_b200 import GradScaler, ZeroAdamW
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=device)
+    try:
+        _, params, groups = _init(device)
+        opt = ZeroAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+        sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+        sc.scale(torch.ones((), device=device))
+        _run(opt, params, sc, device, torch.bfloat16, steps=3, copy_grads=True)
+        sd = opt.consolidated_state_dict()
+        if rank == 0:
+            torch.save({"optimizer": sd, "scaler": sc.state_dict(),
+                        "params": [p.detach().cpu() for p in params]},
+                       os.path.join(out_dir, "zero_ckpt.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@needs_world
+def test_zero_checkpoint_from_n_ranks_resumes_on_one_gpu_bit_exactly(tmp_path):
+    """The sharded checkpoint path (consolidated_state_dict) across an N -> 1 reshard on GPUs:
+    N NCCL ranks take three steps (one with a NaN: skipped) and save the consolidated state in
+    FusedAdamW's per-parameter layout; one GPU loads it into FusedAdamW and takes three more.
+    The result equals one GPU taking all six steps, word for word."""
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler
+    world = WORLDS[0]
+    port = 29700 + os.getpid() % 1000
+    mp.start_processes(_reshard_worker, args=(world, port, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    device = torch.device("cuda", 0)
+    ck = torch.load(tmp_path / "zero_ckpt.pt", weights_only=False)
+
+    def fresh():
+        _, params, groups = _init(device)
+        opt = FusedAdamW(groups, lr=3e-4, betas=(0.9, 0.95), eps=1e-8)
+        sc = GradScaler("cuda", init_scale=2.0 ** 14, growth_interval=2)
+        sc.scale(torch.ones((), device=device))
+        return params, opt, sc
+
+    def continue_from(params, opt, sc, start, steps):
+        for s in range(start, start + steps):
+            for p, g in zip(params, _grads(s, torch.bfloat16, device)):
+                p.grad = g
+            sc.unscale_(opt)
+            from minigpt_train_infra_b200 import clip_grad_norm_
+            clip_grad_norm_(params, 1.0)
+            sc.step(opt)
+            sc.update()
+
+    p1, o1, s1 = fresh()
+    continue_from(p1, o1, s1, 0, 6)
+    p2, o2, s2 = fresh()
+    with torch.no_grad():
+        for p, saved in zip(p2, ck["params"]):
+            p.copy_(saved)
+    o2.load_state_dict(ck["optimizer"])
+    s2.load_state_dict(ck["scaler"])
+    s2.scale(torch.ones((), device=device))
+    continue_from(p2, o2, s2, 3, 3)
+    torch.cuda.synchronize()
+    assert s1.get_scale() == s2.get_scale()
+    for a, b in zip(p1, p2):
+        assert torch.equal(a, b)
+    for a, b in zip(p1, p2):
+        for k in ("step", "exp_avg", "exp_avg_sq", "master_param"):
+            assert torch.equal(o1.state[a][k], o2.state[b][k]), k
