@@ -746,7 +746,8 @@ def run_peer_leg(args, shape_list, P: int, scale: float, std: float, device, pg,
                  rank: int) -> dict:
     """The ZeRO-1 step with the bf16 all-gather fused into the update (``peer_memory=True``):
     the AdamW kernel stores every updated bf16 value into every rank's parameter buffer over
-    NVLink (plain 16-byte stores, no multicast), then a one-element all-reduce orders the ranks.
+    NVLink (TMA bulk stores of staged 4 KB chunks, 16-byte stores for ragged ones), then a
+    one-element all-reduce orders the ranks.
     Timed as the full step -- statistics, norm exchange, update with broadcast, ordering, scaler
     update -- with CUDA events, max over ranks; then checked by the parity leg."""
     import torch.distributed as dist
@@ -785,9 +786,9 @@ def run_peer_leg(args, shape_list, P: int, scale: float, std: float, device, pg,
     bound = _nvlink_bound(opt.geom.padded, opt.local_numel(), ws)
     out = {"ms": round(ms, 4), "gparams_s": round(P / (ms / 1e3) / 1e9, 3), **bound,
            "frac_of_bound": round(bound["bound_ms"] / ms, 4),
-           "note": "statistics + norm exchange + AdamW with the bf16 broadcast fused in (16-byte "
-                   "peer stores over legacy CUDA IPC mappings) + ordering all-reduce + scaler "
-                   "update, per step; max over ranks"}
+           "note": "statistics + norm exchange + AdamW with the bf16 broadcast fused in (bulk "
+                   "stores of staged chunks to legacy CUDA IPC mappings) + ordering all-reduce + "
+                   "scaler update, per step; max over ranks"}
     out["parity"] = parity_check(opt, scaler, step_params, ws, rank, seed=1)
     opt.close()
     return out

@@ -76,6 +76,38 @@ __device__ __forceinline__ float clip_coefficient(float norm, float max_norm) {
   return c > 1.0f ? 1.0f : c;
 }
 
+// TMA bulk stores (the plain shared -> global form of cp.async.bulk, one destination each) of a
+// staged chunk of updated bf16 values to the other ranks' buffers: one instruction per peer
+// moves the whole chunk, so the NVLink writes go out as large contiguous transfers instead of
+// one 16-byte store per lane.
+__device__ __forceinline__ void bulk_store_global(char* dst, const void* smem_src,
+                                                  uint32_t bytes) {
+  uint64_t g;
+  asm volatile("cvta.to.global.u64 %0, %1;" : "=l"(g) : "l"(dst));
+  const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(smem_src));
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               :: "l"(g), "r"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N bulk groups of this thread still read their shared-memory source.
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
+// Waits until every bulk group of this thread has completed (its writes performed).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this CTA's ordinary shared-memory writes before the bulk copies that read them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Largest update chunk the broadcast variant stages in shared memory (elements); the plan's
+// update chunks are 2 Ki elements.  Longer or ragged chunks take the per-lane stores.
+constexpr int kStageElems = 2048;
+
 // Quads (4 consecutive elements) each thread keeps in flight per loop iteration, and the CTAs per
 // SM the register budget is sized for.  Both are build-time knobs; the defaults were measured.
 #ifndef B2O_ADAMW_QUADS
@@ -150,6 +182,11 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
     }
     __syncthreads();
   }
+  // Two shared-memory stages of one chunk's updated bf16 values, for the bulk stores to the
+  // peers (only the broadcast variant with CTA-wide chunk scheduling uses them).
+  constexpr bool kStaged = BCAST && B2O_ADAMW_SCHED != 2;
+  __shared__ __align__(128) uint2 s_stage[kStaged ? 2 : 1][kStaged ? kStageElems / 4 : 1];
+  int sb = 0;
   const float inv = inv_scale_of(loss_scale);
   const float coef = norm_p ? clip_coefficient(*norm_p, max_norm) : 1.0f;
   if (clip_coef_out && blockIdx.x == 0 && threadIdx.x == 0) *clip_coef_out = coef;
@@ -211,6 +248,10 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
     }
     const int64_t n = ch.end - ch.begin;
     int64_t done = 0;
+    // The whole chunk goes to the peers as bulk stores when it fits a stage and is a multiple
+    // of 8 elements (16 bytes); the condition is the same for every thread of the CTA.
+    const bool staged = kStaged && (flags & B2O_FLAG_VECTOR) && n <= kStageElems &&
+                        (n & 7) == 0 && bc.n_ranks > 1;
     if (flags & B2O_FLAG_VECTOR) {
       const int64_t nq = n >> 2;
       done = nq << 2;
@@ -252,7 +293,12 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
               pq.x = pack_bf16x2(wf[0], wf[1]);
               pq.y = pack_bf16x2(wf[2], wf[3]);
               __stcs(reinterpret_cast<uint2*>(pp + e), pq);
-              if (BCAST) broadcast_quad(bc, s_peer, pp + e, pq, q, nq, lane);
+              if (BCAST) {
+                if (staged)
+                  s_stage[kStaged ? sb : 0][q] = pq;
+                else
+                  broadcast_quad(bc, s_peer, pp + e, pq, q, nq, lane);
+              }
             }
           }
         }
@@ -277,6 +323,20 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
         }
       }
     }
+    if (kStaged && staged) {
+      __syncthreads();  // the whole chunk is in s_stage[sb]
+      if (threadIdx.x == 0) {
+        fence_proxy_async_smem();
+        const int64_t byte = reinterpret_cast<const char*>(pp + ch.begin) - bc.my_base;
+        const uint32_t bytes = uint32_t(n) * 2u;
+        for (int j = 0; j < bc.n_ranks - 1; ++j)
+          bulk_store_global(s_peer[j] + byte, &s_stage[sb][0], bytes);
+        bulk_commit();
+        bulk_wait_read<1>();  // the group of the chunk before this one has read s_stage[sb ^ 1]
+      }
+      __syncthreads();  // s_stage[sb ^ 1] may be written again
+      sb ^= 1;
+    }
 #if B2O_ADAMW_SCHED == 1
     __syncthreads();  // s_tile[buf ^ 1] is written; every thread moves on together
     buf ^= 1;
@@ -287,6 +347,7 @@ adamw_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
   }
 
   // Completion ticket; the last CTA advances the step counters after every CTA has read them.
+  if (kStaged && threadIdx.x == 0) bulk_wait_all();  // the bulk stores to the peers are done
   if (BCAST) __threadfence_system();  // peer stores performed before the kernel completes
   __threadfence();
   __syncthreads();
