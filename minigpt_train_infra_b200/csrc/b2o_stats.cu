@@ -9,9 +9,10 @@
 // Reduction order (deterministic for a given plan and grid):
 //   element -> fp32 sum of squares over one 8-element vector (fma chain)
 //   vector  -> fp64 per-thread sum -> fixed-order CTA sum = one fp64 partial per chunk
-//   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order with a
-//              fixed lane-strided walk + xor-shuffle tree into exch[slot] (a tensor of one
-//              chunk: its partial, copied by one thread -- the same value the walk gives)
+//   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order: a
+//              tensor of one chunk is its partial (copied by one thread); up to 512 chunks, a
+//              fixed lane-strided walk + xor-shuffle tree of one warp; more, a fixed
+//              thread-strided walk + the CTA tree of the whole CTA; the result goes to exch[slot]
 //   slot    -> per-tensor norm fp32(sqrt(sum)), total fp32(sqrt(sum of squared norms)); the
 //              same two-level structure as clip_grad.py:_get_total_norm.
 #include <cuda.h>
@@ -45,6 +46,10 @@ __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slo
   }
 }
 
+// Tensors with more chunk partials than this are folded by a whole CTA at the end of the pass,
+// the others by one warp.
+constexpr int kWarpFoldMax = 512;
+
 // End of a statistics pass, executed by every thread of every CTA after its chunk loop: record
 // the CTA's non-finite flag, take a completion ticket, and let the CTA holding the last ticket
 // fold the chunk partials (per tensor, in chunk order) into exch, then optionally finish the norm.
@@ -69,9 +74,11 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
   __syncthreads();
   // Every thread loads the table entry of one tensor (warp w, lane l: tensor w + kWarps * l of
   // each block of kWarps * 32).  A tensor of at most one chunk is finished by that thread: its
-  // sum is its one partial (or 0).  Longer tensors are folded by their warp, one at a time: each
-  // lane sums the chunk partials k, k+32, k+64, ... in that order, with eight loads in flight
-  // before the additions, then the warp's xor tree adds the 32 lane sums.
+  // sum is its one partial (or 0).  Tensors of up to kWarpFoldMax chunks are folded by their
+  // warp, one at a time: each lane sums the chunk partials k, k+32, k+64, ... in that order, with
+  // eight loads in flight before the additions, then the warp's xor tree adds the 32 lane sums.
+  // Longer tensors are folded afterwards by the whole CTA (below).  Which fold a tensor gets
+  // depends only on its chunk count, so the result is deterministic.
   for (int base = 0; base < n_tensors; base += kWarps * 32) {
     const int mine = base + lane * kWarps + warp;
     int my_begin = 0, my_count = 0, my_slot = 0;
@@ -81,7 +88,8 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
       my_slot = tensors[mine].slot;
       if (my_count <= 1) exch[my_slot] = my_count ? __ldcg(ws.chunk_sums + my_begin) : 0.0;
     }
-    unsigned int multi = __ballot_sync(0xffffffffu, mine < n_tensors && my_count > 1);
+    unsigned int multi = __ballot_sync(0xffffffffu, mine < n_tensors && my_count > 1 &&
+                                                        my_count <= kWarpFoldMax);
     while (multi) {
       const int j = __ffs(multi) - 1;
       multi &= multi - 1;
@@ -102,6 +110,40 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
       sum = warp_sum(sum);
       if (lane == 0) exch[slot] = sum;
     }
+  }
+  // Tensors of more than kWarpFoldMax chunks, one after another, each by the whole CTA: thread t
+  // sums the partials t, t + kThreads, ... in that order (eight loads in flight), then the fixed
+  // CTA tree.  A large tensor's partials are then read in a few rounds instead of one warp's
+  // many, which shortens the single-CTA tail of the pass.
+  __shared__ unsigned int s_big[kWarps];
+  for (int base = 0; base < n_tensors; base += kThreads) {
+    const int i = base + threadIdx.x;
+    const bool big = i < n_tensors && tensors[i].chunk_count > kWarpFoldMax;
+    const unsigned int ballot = __ballot_sync(0xffffffffu, big);
+    if (lane == 0) s_big[warp] = ballot;
+    __syncthreads();
+    for (int w = 0; w < kWarps; ++w) {
+      unsigned int m = s_big[w];
+      while (m) {
+        const int j = base + w * 32 + __ffs(m) - 1;
+        m &= m - 1;
+        const int count = tensors[j].chunk_count;
+        const double* part = ws.chunk_sums + tensors[j].chunk_begin;
+        double sum = 0.0;
+        int k = threadIdx.x;
+        for (; k + 7 * kThreads < count; k += 8 * kThreads) {
+          double a[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) a[u] = __ldcg(part + k + u * kThreads);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) sum += a[u];
+        }
+        for (; k < count; k += kThreads) sum += __ldcg(part + k);
+        const double total = block_sum(sum, scratch);
+        if (threadIdx.x == 0) exch[tensors[j].slot] = total;
+      }
+    }
+    __syncthreads();  // s_big is rewritten for the next block of the table
   }
   if (threadIdx.x == 0) {
     const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
