@@ -85,6 +85,7 @@ def grad_signature(grads: list) -> tuple:
         return (tuple(map(_data_ptr, act)), tuple(map(_version_of, act)),
                 tuple(i for i, g in enumerate(grads) if g is None))
 
+
 STALE_STATS_MESSAGE = (
     "gradients were modified after this package's GradScaler.unscale_() / clip_grad_norm_() "
     "took their statistics, so the recorded loss scale, non-finite flag and norm no longer "
@@ -222,6 +223,7 @@ class FusedAdamW(torch.optim.Optimizer):
                 raise RuntimeError(STALE_STATS_MESSAGE)
         else:
             plans = self._prepare()
+            self._last_grads = []
         if not plans:
             return loss
         store = self._store
@@ -297,6 +299,7 @@ class FusedAdamW(torch.optim.Optimizer):
         if not self._capturable():
             raise RuntimeError("construct the optimizer with capturable=True to replay it")
         self._prepare()
+        self._last_grads = []
         self.stage_hyperparams()
 
     def state_dict(self) -> dict[str, Any]:
@@ -382,6 +385,7 @@ class FusedAdamW(torch.optim.Optimizer):
                                   (grad_signature([p.grad for p in self._store.params])
                                    if self._store is not None else ()),
                                   plans=plans)
+        self._last_grads = []  # hold no gradient past this call (zero_grad may free them)
         return self._pending
 
     def _owns_exactly(self, params: list[torch.Tensor]) -> bool:
@@ -506,7 +510,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self._sync_state()
         params = store.params
         grads = [p.grad for p in params]
-        self._last_grads = grads
+        self._last_grads = grads  # for the caller's gradient signature; it clears the list
         try:
             gptr = tuple(map(_data_ptr, grads))
         except TypeError:  # some parameters have no gradient

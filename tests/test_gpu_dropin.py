@@ -372,3 +372,29 @@ def test_step_hooks_and_profiler_range_as_torch_provides_them():
     assert "Optimizer.step#FusedAdamW.step" in names
     torch.cuda.synchronize()
     assert float(opt.state[params[0]]["step"]) == 4.0
+
+
+def test_no_gradient_is_held_after_the_step():
+    """A loop that frees its gradients (zero_grad(set_to_none=True), train.py:465) must get their
+    memory back before the next backward: nothing of the optimizer, scaler or clip keeps a
+    reference to a gradient once the step is done."""
+    import gc
+    import weakref
+    from minigpt_train_infra_b200 import FusedAdamW, GradScaler, clip_grad_norm_
+    shapes = [(64, 32), (32,)]
+    _, params = _params(shapes, torch.bfloat16, seed=8)
+    opt = FusedAdamW(params, lr=1e-3)
+    sc = GradScaler("cuda", init_scale=2.0 ** 8)
+    sc.scale(torch.ones((), device=DEV))
+    refs = []
+    for s in range(3):
+        for p, g in zip(params, _grads(shapes, s, torch.bfloat16, 2.0 ** 8)):
+            p.grad = g.to(DEV)
+        refs.append([weakref.ref(p.grad) for p in params])
+        sc.unscale_(opt)
+        clip_grad_norm_(params, 1.0)
+        sc.step(opt)
+        sc.update()
+        opt.zero_grad(set_to_none=True)
+        gc.collect()
+        assert all(r() is None for r in refs[-1])
