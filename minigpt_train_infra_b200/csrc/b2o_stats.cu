@@ -9,15 +9,18 @@
 // Reduction order (deterministic for a given plan and grid):
 //   element -> fp32 sum of squares over one 8-element vector (fma chain)
 //   vector  -> fp64 per-thread sum -> fixed-order CTA sum = one fp64 partial per chunk
-//   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order: a
-//              tensor of one chunk is its partial (copied by one thread); up to 512 chunks, a
-//              fixed lane-strided walk + xor-shuffle tree of one warp; more, a fixed
-//              thread-strided walk + the CTA tree of the whole CTA; the result goes to exch[slot]
+//   chunk   -> the last CTA to finish folds each tensor's chunk partials in chunk order,
+//              staged in shared memory 4096 at a time: a tensor's piece of at most 128
+//              partials by one thread (four interleaved accumulators, then (a0+a1)+(a2+a3)),
+//              a longer piece by one warp (fixed lane-strided walk + xor-shuffle tree), the
+//              pieces of a tensor that spans windows added in window order; the result goes to
+//              exch[slot]
 //   slot    -> per-tensor norm fp32(sqrt(sum)), total fp32(sqrt(sum of squared norms)); the
 //              same two-level structure as clip_grad.py:_get_total_norm.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <mutex>
 
 #include "b2o_device.cuh"
@@ -29,6 +32,10 @@ namespace b2o {
 __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slots,
                                   float* found_inf_out, float* norm_out, double* scratch) {
   const int stride = n_slots + 1;
+  // Thread 0 reads the non-finite counts first, so their latency overlaps the slot loop.
+  double bad = 0.0;
+  if (threadIdx.x == 0)
+    for (int r = 0; r < n_ranks; ++r) bad += __ldcg(exch_all + (int64_t)r * stride + n_slots);
   double local = 0.0;
   for (int s = threadIdx.x; s < n_slots; s += blockDim.x) {
     double sum = 0.0;
@@ -39,24 +46,30 @@ __device__ void finalize_norm_cta(const double* exch_all, int n_ranks, int n_slo
   }
   const double total_sq = block_sum(local, scratch);
   if (threadIdx.x == 0) {
-    double bad = 0.0;
-    for (int r = 0; r < n_ranks; ++r) bad += __ldcg(exch_all + (int64_t)r * stride + n_slots);
     if (found_inf_out) *found_inf_out = bad != 0.0 ? 1.0f : 0.0f;
     if (norm_out) *norm_out = (float)sqrt(total_sq);
   }
 }
 
-// Tensors with more chunk partials than this are folded by a whole CTA at the end of the pass,
-// the others by one warp.
-constexpr int kWarpFoldMax = 512;
+// The final fold stages the chunk partials in shared memory, kFoldWin at a time: each thread
+// keeps kFoldLoads loads in flight, and the loads of the next window are issued before the
+// current window is folded, so the fold costs about one L2 round trip per window instead of
+// one per tensor.  Within a window the tensors are folded in parallel: a piece of at most
+// kThreadFoldMax partials by the thread holding its tensor, a longer one by a warp.
+constexpr int kFoldWin = 4096;
+constexpr int kFoldLoads = kFoldWin / kThreads;
+constexpr int kThreadFoldMax = 128;
+static_assert(kFoldWin % kThreads == 0, "whole loads per thread");
+static_assert(kWarps == 8, "a long piece's warp is picked with a mask of every 8th bit");
 
 // End of a statistics pass, executed by every thread of every CTA after its chunk loop: record
 // the CTA's non-finite flag, take a completion ticket, and let the CTA holding the last ticket
 // fold the chunk partials (per tensor, in chunk order) into exch, then optionally finish the norm.
 __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __restrict__ tensors,
-                                               int n_tensors, int n_slots, Workspace ws,
-                                               double* exch, int flags, float* found_inf_out,
-                                               float* norm_out, double* scratch, int* is_last_p) {
+                                               int n_tensors, int64_t n_chunks, int n_slots,
+                                               Workspace ws, double* exch, int flags,
+                                               float* found_inf_out, float* norm_out,
+                                               double* scratch, int* is_last_p) {
   int& is_last = *is_last_p;
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(ws.stats_nonfinite, 1u);
 
@@ -68,91 +81,153 @@ __device__ __forceinline__ void stats_epilogue(bool bad, const b2o_tensor* __res
   if (!is_last) return;
   __threadfence();
 
+  __shared__ double s_part[kFoldWin];     // the window's chunk partials
+  __shared__ double s_acc[kThreads];      // running sum of a tensor whose chunks span windows
+  __shared__ int s_begin[kThreads], s_end[kThreads], s_slot[kThreads];  // one block of the table
+  __shared__ unsigned int s_mask[kWarps];  // tensors of the block with a long piece in the window
+  __shared__ int s_lo, s_hi;
+
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (flags & B2O_STATS_CLEAR)
-    for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
-  __syncthreads();
-  // Every thread loads the table entry of one tensor (warp w, lane l: tensor w + kWarps * l of
-  // each block of kWarps * 32).  A tensor of at most one chunk is finished by that thread: its
-  // sum is its one partial (or 0).  Tensors of up to kWarpFoldMax chunks are folded by their
-  // warp, one at a time: each lane sums the chunk partials k, k+32, k+64, ... in that order, with
-  // eight loads in flight before the additions, then the warp's xor tree adds the 32 lane sums.
-  // Longer tensors are folded afterwards by the whole CTA (below).  Which fold a tensor gets
-  // depends only on its chunk count, so the result is deterministic.
-  for (int base = 0; base < n_tensors; base += kWarps * 32) {
-    const int mine = base + lane * kWarps + warp;
-    int my_begin = 0, my_count = 0, my_slot = 0;
-    if (mine < n_tensors) {
-      my_begin = tensors[mine].chunk_begin;
-      my_count = tensors[mine].chunk_count;
-      my_slot = tensors[mine].slot;
-      if (my_count <= 1) exch[my_slot] = my_count ? __ldcg(ws.chunk_sums + my_begin) : 0.0;
-    }
-    unsigned int multi = __ballot_sync(0xffffffffu, mine < n_tensors && my_count > 1 &&
-                                                        my_count <= kWarpFoldMax);
-    while (multi) {
-      const int j = __ffs(multi) - 1;
-      multi &= multi - 1;
-      const int begin = __shfl_sync(0xffffffffu, my_begin, j);
-      const int count = __shfl_sync(0xffffffffu, my_count, j);
-      const int slot = __shfl_sync(0xffffffffu, my_slot, j);
-      const double* part = ws.chunk_sums + begin;
-      double sum = 0.0;
-      int k = lane;
-      for (; k + 7 * 32 < count; k += 8 * 32) {
-        double a[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) a[u] = __ldcg(part + k + u * 32);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) sum += a[u];
-      }
-      for (; k < count; k += 32) sum += __ldcg(part + k);
-      sum = warp_sum(sum);
-      if (lane == 0) exch[slot] = sum;
-    }
-  }
-  // Tensors of more than kWarpFoldMax chunks, one after another, each by the whole CTA: thread t
-  // sums the partials t, t + kThreads, ... in that order (eight loads in flight), then the fixed
-  // CTA tree.  A large tensor's partials are then read in a few rounds instead of one warp's
-  // many, which shortens the single-CTA tail of the pass.
-  __shared__ unsigned int s_big[kWarps];
-  for (int base = 0; base < n_tensors; base += kThreads) {
-    const int i = base + threadIdx.x;
-    const bool big = i < n_tensors && tensors[i].chunk_count > kWarpFoldMax;
-    const unsigned int ballot = __ballot_sync(0xffffffffu, big);
-    if (lane == 0) s_big[warp] = ballot;
-    __syncthreads();
-    for (int w = 0; w < kWarps; ++w) {
-      unsigned int m = s_big[w];
-      while (m) {
-        const int j = base + w * 32 + __ffs(m) - 1;
-        m &= m - 1;
-        const int count = tensors[j].chunk_count;
-        const double* part = ws.chunk_sums + tensors[j].chunk_begin;
-        double sum = 0.0;
-        int k = threadIdx.x;
-        for (; k + 7 * kThreads < count; k += 8 * kThreads) {
-          double a[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) a[u] = __ldcg(part + k + u * kThreads);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) sum += a[u];
-        }
-        for (; k < count; k += kThreads) sum += __ldcg(part + k);
-        const double total = block_sum(sum, scratch);
-        if (threadIdx.x == 0) exch[tensors[j].slot] = total;
-      }
-    }
-    __syncthreads();  // s_big is rewritten for the next block of the table
-  }
+  // Every CTA has set its non-finite bit and taken its ticket: the flag and both counters are
+  // final, so they are taken and reset now and the exchange's latency overlaps the fold.
+  unsigned int nonfinite = 0;
   if (threadIdx.x == 0) {
-    const unsigned int nf = atomicExch(ws.stats_nonfinite, 0u);
-    if (nf) exch[n_slots] += 1.0;
+    nonfinite = atomicExch(ws.stats_nonfinite, 0u);
     *ws.stats_tile = 0u;
     *ws.stats_done = 0u;
   }
-  __threadfence();
-  __syncthreads();
+  if (flags & B2O_STATS_CLEAR)
+    for (int s = threadIdx.x; s <= n_slots; s += kThreads) exch[s] = 0.0;
+  const int n_part = int(n_chunks);  // the planner keeps chunk counts below 2**31
+
+  // The table is taken in blocks of kThreads tensors, thread t holding tensor base + t.  The
+  // partials of a block's tensors are staged window by window over [lo, hi), the span of their
+  // chunk ranges.  A tensor's piece of a window is summed in chunk order, by one of two fixed
+  // rules chosen by the piece's length alone:
+  //   at most kThreadFoldMax partials: by the tensor's thread, partial i of the piece into
+  //     accumulator i % 4, then (a0 + a1) + (a2 + a3);
+  //   longer: by warp t % kWarps, lane l summing partials l, l + 32, ... in that order, then the
+  //     warp's xor tree.  A warp takes its long pieces as soon as its own short ones are done.
+  // A tensor whose chunks span windows adds its windows' sums in window order.  The result
+  // depends only on the plan, so it is deterministic.
+  double a[kFoldLoads];
+  // The first window of the first block is almost always [0, ...): its loads are issued before
+  // the table is read, and issued again below only if the table says otherwise.
+  int staged_from = 0;
+#pragma unroll
+  for (int u = 0; u < kFoldLoads; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    a[u] = i < n_part ? __ldcg(ws.chunk_sums + i) : 0.0;
+  }
+  for (int base = 0; base < n_tensors; base += kThreads) {
+    const int nt = min(kThreads, n_tensors - base);
+    if (threadIdx.x == 0) {
+      s_lo = INT_MAX;
+      s_hi = 0;
+    }
+    __syncthreads();  // also orders the CLEAR stores and the previous block before this one
+    int tb = 0, te = 0, slot = 0;
+    if (threadIdx.x < nt) {
+      const b2o_tensor& t = tensors[base + threadIdx.x];
+      tb = max(t.chunk_begin, 0);
+      te = min(t.chunk_begin + t.chunk_count, n_part);
+      slot = t.slot;
+      s_begin[threadIdx.x] = tb;
+      s_end[threadIdx.x] = te;
+      s_slot[threadIdx.x] = slot;
+      if (te <= tb) {
+        exch[slot] = 0.0;  // a tensor with no chunks
+      } else {
+        atomicMin(&s_lo, tb);
+        atomicMax(&s_hi, te);
+      }
+    }
+    __syncthreads();
+    const int lo = s_lo, hi = s_hi;  // lo > hi when no tensor of the block has a chunk
+    if (lo < hi && lo != staged_from) {
+#pragma unroll
+      for (int u = 0; u < kFoldLoads; ++u) {
+        const int64_t i = int64_t(lo) + threadIdx.x + u * kThreads;
+        a[u] = i < hi ? __ldcg(ws.chunk_sums + i) : 0.0;
+      }
+    }
+    staged_from = -1;  // later blocks always load their first window here
+    for (int w0 = lo; w0 < hi; w0 += kFoldWin) {
+      const int w1 = min(w0 + kFoldWin, hi);
+      const int pb = max(tb, w0), pe = min(te, w1);  // this thread's tensor's piece
+      const bool has = tb < te && pb < pe;
+      const bool is_long = has && pe - pb > kThreadFoldMax;
+      const unsigned int m = __ballot_sync(0xffffffffu, is_long);
+      if (lane == 0) s_mask[warp] = m;
+#pragma unroll
+      for (int u = 0; u < kFoldLoads; ++u) {
+        const int i = threadIdx.x + u * kThreads;
+        if (w0 + i < w1) s_part[i] = a[u];
+      }
+      __syncthreads();
+      if (w1 < hi) {
+#pragma unroll
+        for (int u = 0; u < kFoldLoads; ++u) {
+          const int64_t i = int64_t(w1) + threadIdx.x + u * kThreads;
+          a[u] = i < hi ? __ldcg(ws.chunk_sums + i) : 0.0;
+        }
+      }
+      if (has && !is_long) {
+        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+        int j = pb - w0;
+        const int je = pe - w0;
+#pragma unroll 2
+        for (; j + 3 < je; j += 4) {
+          a0 += s_part[j];
+          a1 += s_part[j + 1];
+          a2 += s_part[j + 2];
+          a3 += s_part[j + 3];
+        }
+        if (j < je) a0 += s_part[j];
+        if (j + 1 < je) a1 += s_part[j + 1];
+        if (j + 2 < je) a2 += s_part[j + 2];
+        const double sum = (a0 + a1) + (a2 + a3);
+        const double acc = pb > tb ? s_acc[threadIdx.x] + sum : sum;
+        if (pe < te)
+          s_acc[threadIdx.x] = acc;
+        else
+          exch[slot] = acc;
+      }
+      for (int q = 0; q < kWarps; ++q) {
+        unsigned int mm = s_mask[q] & (0x01010101u << warp);  // tensors q*32 + warp + 8k
+        while (mm) {
+          const int p = q * 32 + __ffs(mm) - 1;
+          mm &= mm - 1;
+          const int b = max(s_begin[p], w0), e = min(s_end[p], w1);
+          // four loads in flight before the additions, which stay in partial order
+          double sum = 0.0;
+          int j = b - w0 + lane;
+          const int je = e - w0;
+          for (; j + 3 * 32 < je; j += 4 * 32) {
+            const double x0 = s_part[j], x1 = s_part[j + 32];
+            const double x2 = s_part[j + 64], x3 = s_part[j + 96];
+            sum += x0;
+            sum += x1;
+            sum += x2;
+            sum += x3;
+          }
+          for (; j < je; j += 32) sum += s_part[j];
+          sum = warp_sum(sum);
+          if (lane == 0) {
+            const double acc = b > s_begin[p] ? s_acc[p] + sum : sum;
+            if (e < s_end[p])
+              s_acc[p] = acc;
+            else
+              exch[s_slot[p]] = acc;
+          }
+        }
+      }
+      __syncthreads();  // s_part, s_mask and s_acc are written again in the next window
+    }
+  }
+  __syncthreads();  // after the CLEAR stores even when the table is empty
+  if (threadIdx.x == 0 && nonfinite) exch[n_slots] += 1.0;
+  __syncthreads();  // the CTA's exch stores are visible to the CTA's finalize loads
   if (flags & B2O_STATS_FINALIZE)
     finalize_norm_cta(exch, 1, n_slots, found_inf_out, norm_out, scratch);
 }
@@ -169,7 +244,7 @@ template <> struct StatsUnroll<GradF32> { static constexpr int value = 4; };
 #endif
 
 template <class G, int U = StatsUnroll<G>::value>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
                   const b2o_chunk* __restrict__ chunks, int64_t n_chunks, int n_slots,
                   const float* __restrict__ loss_scale, Workspace ws, double* exch,
@@ -245,8 +320,8 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
 #endif
   }
 
-  stats_epilogue(bad, tensors, n_tensors, n_slots, ws, exch, flags, found_inf_out, norm_out,
-                 scratch, &is_last);
+  stats_epilogue(bad, tensors, n_tensors, n_chunks, n_slots, ws, exch, flags, found_inf_out,
+                 norm_out, scratch, &is_last);
 }
 
 // Reduce-scatter of bf16 gradients fused with the statistics pass.  Each element of this rank's
@@ -254,7 +329,7 @@ grad_stats_kernel(const b2o_tensor* __restrict__ tensors, int n_tensors,
 // rounded to bf16 and written in place; the statistics are taken on the rounded values, i.e. on
 // exactly what the update pass will read.
 template <int U>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 rs_stats_kernel(PeerPtrs peers, int n_ranks, const char* my_base, float scale_factor,
                 const b2o_tensor* __restrict__ tensors, int n_tensors,
                 const b2o_chunk* __restrict__ chunks, int64_t n_chunks, int n_slots,
@@ -346,11 +421,11 @@ rs_stats_kernel(PeerPtrs peers, int n_ranks, const char* my_base, float scale_fa
     buf ^= 1;
     c = s_tile[buf];
   }
-  stats_epilogue(bad, tensors, n_tensors, n_slots, ws, exch, B2O_STATS_CLEAR, nullptr, nullptr,
-                 scratch, &is_last);
+  stats_epilogue(bad, tensors, n_tensors, n_chunks, n_slots, ws, exch, B2O_STATS_CLEAR, nullptr,
+                 nullptr, scratch, &is_last);
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 finalize_norm_kernel(const double* exch_all, int n_ranks, int n_slots, float* found_inf_out,
                      float* norm_out) {
   __shared__ double scratch[kWarps];
